@@ -1,0 +1,218 @@
+/*
+ * xrgpu_mmnb.h -- C ABI of the B200 (sm_100a) backend for com.microsoft.MatMulNBits.
+ *
+ *   Y[M, N] = A[M, K] . dequant(B)^T (+ bias),
+ *   dequant(B)[n, k] = (float(q[n, k]) - z[n, k / bs]) * scales[n, k / bs],
+ *
+ * B is uint8 [N, ceil(K/bs), ceil(bs*bits/8)] with codes packed low-first, bits in {2,4,8}.
+ *
+ * Two call styles:
+ *   1. The operator API of the reference backend (prepare / run / read_outputs / info / close)
+ *      over named host tensors, mirroring xrgpu::operators::extended
+ *      (runtime/include/xrgpu/extended_operators.h:22-61, runtime/include/xrgpu/operators.h:9-55).
+ *   2. A zero-copy call over device pointers on a caller's CUDA stream (xrgpu_mmnb_forward).
+ *
+ * Every function returns an xrgpu_status; on failure xrgpu_last_error() holds a message
+ * (thread-local). No function falls back to CPU computation.
+ */
+#ifndef XRGPU_MMNB_H
+#define XRGPU_MMNB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define XRGPU_API __attribute__((visibility("default")))
+#else
+#define XRGPU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Logical dtypes, same numbering as xrgpu::operators::DType (operators.h:9). */
+typedef enum {
+  XRGPU_FLOAT32 = 0,
+  XRGPU_FLOAT16 = 1,
+  XRGPU_INT32 = 2,
+  XRGPU_UINT32 = 3,
+  XRGPU_INT16 = 4,
+  XRGPU_INT8 = 5,
+  XRGPU_UINT8 = 6,
+  XRGPU_INT64 = 7,
+  XRGPU_BOOL = 8,
+  XRGPU_UNSPECIFIED = 9
+} xrgpu_dtype;
+
+/* Status codes in place of the reference's exceptions:
+ *   XRGPU_INVALID_ARGUMENT  <- std::invalid_argument (contracts.cpp:9-20, complex_plan.cpp:52-120,
+ *                              planner.cpp:12-99)
+ *   XRGPU_RUNTIME_ERROR     <- std::runtime_error (vulkan.cpp:24-26, 115); also a poisoned handle
+ *   XRGPU_TIMEOUT           <- the fence wait exceeding Options.timeout_ns (vulkan.cpp:115)
+ *   XRGPU_DEVICE_ERROR      <- a nonzero device error word (vulkan.cpp:115 "contract validation failed")
+ *   XRGPU_UNAVAILABLE       <- no usable CUDA device (operators.h:34 probe: available=false)        */
+typedef enum {
+  XRGPU_OK = 0,
+  XRGPU_INVALID_ARGUMENT = 1,
+  XRGPU_RUNTIME_ERROR = 2,
+  XRGPU_TIMEOUT = 3,
+  XRGPU_DEVICE_ERROR = 4,
+  XRGPU_UNAVAILABLE = 5
+} xrgpu_status;
+
+#define XRGPU_MAX_RANK 16
+
+/* Named tensor: xrgpu::operators::Tensor (operators.h:16-23). Logical dtype, shape and
+ * contiguous little-endian row-major bytes. For xrgpu_prepare, data is a HOST pointer. */
+typedef struct {
+  const char* name;
+  int32_t dtype;                 /* xrgpu_dtype */
+  int32_t rank;
+  int64_t shape[XRGPU_MAX_RANK];
+  const void* data;
+  uint64_t nbytes;
+} xrgpu_tensor;
+
+/* One integer attribute (MatMulNBits has integer attributes only: K, N, bits, block_size,
+ * accuracy_level; contract.json:2-40). */
+typedef struct {
+  const char* name;
+  int64_t value;
+} xrgpu_int_attr;
+
+/* extended::Request (extended_operators.h:22-28). args override attrs (planner.cpp:72-85). */
+typedef struct {
+  const char* operation;         /* "com.microsoft.MatMulNBits" */
+  const xrgpu_tensor* inputs;
+  int32_t num_inputs;
+  const xrgpu_int_attr* attrs;
+  int32_t num_attrs;
+  const xrgpu_int_attr* args;
+  int32_t num_args;
+} xrgpu_request;
+
+/* xrgpu::operators::Options (operators.h:24-28) plus the CUDA device ordinal. */
+typedef struct {
+  int32_t profiling;             /* nonzero: time each run() with CUDA events (info "gpu_ms") */
+  uint64_t timeout_ns;           /* bound on run()'s wait; default 15 s */
+  uint64_t memory_limit_bytes;   /* bound on device bytes prepare() may hold; default 256 MiB */
+  int32_t device;                /* CUDA device ordinal; default 0 */
+} xrgpu_options;
+
+typedef struct xrgpu_operator xrgpu_operator;
+
+/* Message of the last failure on the calling thread ("" when none). */
+XRGPU_API const char* xrgpu_last_error(void);
+
+/* Fills o with the reference defaults (operators.h:24-28): profiling off, 15 s, 256 MiB, device 0. */
+XRGPU_API void xrgpu_default_options(xrgpu_options* o);
+
+/* JSON {"available","backend","device","reason",...}; replaces operators.h:34 probe().
+ * Writes at most capacity bytes (NUL-terminated); *needed (if non-NULL) gets the full size. */
+XRGPU_API int xrgpu_probe(char* json, uint64_t capacity, uint64_t* needed);
+
+/* Metadata-only validation and output inference; replaces extended::plan(Request)
+ * (extended_operators.h:48, planner.cpp:67 -> complex_plan.cpp:58,117-120). Reads no
+ * tensor bytes. outputs[0] receives yT's name/dtype/rank/shape (data NULL, nbytes set). */
+XRGPU_API int xrgpu_plan(const xrgpu_request* request, xrgpu_tensor* outputs, int32_t capacity, int32_t* count);
+
+/* Validates, plans and copies every input to the device; replaces Operator::prepare
+ * (extended_operators.h:51, vulkan.cpp:109-114,119). package_directory is accepted for
+ * signature parity and may be NULL (kernels are linked into this library). */
+XRGPU_API int xrgpu_prepare(const char* package_directory, const xrgpu_request* request,
+                  const xrgpu_options* options, xrgpu_operator** out);
+
+/* Synchronous execution bounded by options.timeout_ns; replaces Operator::run (vulkan.cpp:115,120).
+ * A failure poisons the handle until xrgpu_close (vulkan.cpp:105). */
+XRGPU_API int xrgpu_run(xrgpu_operator* op);
+
+/* Copies output `index` (0 = yT) to host memory; replaces Operator::read_outputs (vulkan.cpp:121). */
+XRGPU_API int xrgpu_read_outputs(const xrgpu_operator* op, int32_t index, void* dst, uint64_t capacity);
+
+/* JSON statistics; replaces Operator::info (vulkan.cpp:123): backend, operation, device,
+ * execution_ms, gpu_ms, dispatch_count, path, cpu_compute_fallback (always false), closed. */
+XRGPU_API int xrgpu_info(const xrgpu_operator* op, char* json, uint64_t capacity, uint64_t* needed);
+
+/* Waits for submitted work and releases device memory; replaces Operator::close (vulkan.cpp:122).
+ * The handle stays valid for xrgpu_info until xrgpu_destroy. */
+XRGPU_API int xrgpu_close(xrgpu_operator* op);
+
+/* Frees the handle (closing it first if needed); the reference's ~Operator. */
+XRGPU_API void xrgpu_destroy(xrgpu_operator* op);
+
+/* Extension (no reference counterpart): replaces the bytes of one prepared input of the same
+ * name, dtype and size (e.g. a new activation for the next decode step) without re-preparing
+ * the weights. Host pointer; the copy completes before return. */
+XRGPU_API int xrgpu_write_input(xrgpu_operator* op, const char* name, const void* data, uint64_t nbytes);
+
+/* Extension: enqueue run() on `stream` (cudaStream_t; NULL = the handle's own stream)
+ * without waiting. Errors raised on the device surface at the next xrgpu_run/xrgpu_sync. */
+XRGPU_API int xrgpu_run_async(xrgpu_operator* op, void* stream);
+
+/* Extension: waits for the handle's work; checks the device error word. */
+XRGPU_API int xrgpu_sync(xrgpu_operator* op);
+
+/* Extension: device pointer of output `index` (valid until xrgpu_close). */
+XRGPU_API int xrgpu_output_device_ptr(const xrgpu_operator* op, int32_t index, void** ptr);
+
+/* ---------------------------------------------------------------------------------------
+ * Zero-copy device API (extension). Pointers are device pointers of the current context.
+ * ------------------------------------------------------------------------------------- */
+
+/* Kernel selection for xrgpu_mmnb_forward (the planner's choice unless forced). */
+typedef enum {
+  XRGPU_PATH_AUTO = 0,
+  XRGPU_PATH_GENERIC = 1,   /* any bits/block size/dtype; float32 CUDA-core accumulation */
+  XRGPU_PATH_GEMV = 2,      /* 4-bit decode GEMV, M <= 16, float16 A */
+  XRGPU_PATH_GEMM = 3       /* 4-bit prefill GEMM on tcgen05 tensor cores, float16 A */
+} xrgpu_mmnb_path;
+
+typedef struct {
+  int32_t dtype;            /* T1 of aT/scalesT/biasT/yT: XRGPU_FLOAT32 or XRGPU_FLOAT16 */
+  int32_t zero_point_dtype; /* XRGPU_UNSPECIFIED: absent (z = 2^(bits-1));
+                               XRGPU_FLOAT32 / XRGPU_FLOAT16: [N, ceil(K/bs)] (reference contract);
+                               XRGPU_UINT8: packed [N, ceil(ceil(K/bs)*bits/8)] (ONNX Runtime form) */
+  int32_t path;             /* xrgpu_mmnb_path */
+  int32_t reserved;
+  int64_t M, K, N, block_size, bits;
+  const void* a;            /* [M, K] T1 */
+  const uint8_t* b;         /* [N, ceil(K/bs), ceil(bs*bits/8)] */
+  const void* scales;       /* [N, ceil(K/bs)] T1 */
+  const void* zero_points;  /* see zero_point_dtype; NULL when absent */
+  const void* bias;         /* [N] T1 or NULL */
+  void* y;                  /* [M, ldy] T1 */
+  int64_t ldy;              /* row stride of y in elements; 0 means N */
+} xrgpu_mmnb_problem;
+
+/* Device scratch bytes xrgpu_mmnb_forward needs for this problem (split-K partial sums and
+ * tile counters; may be 0). */
+XRGPU_API int xrgpu_mmnb_workspace_size(const xrgpu_mmnb_problem* p, uint64_t* bytes);
+
+/* Enqueues Y = A.dequant(B)^T (+bias) on `stream` (cudaStream_t, NULL = legacy default).
+ * workspace: device scratch of at least xrgpu_mmnb_workspace_size bytes, zero-filled before its
+ * first use and left zero-filled by every completed call; NULL = a per-device workspace owned by
+ * the library (grown on demand, so that call may allocate). Calls sharing a workspace must not
+ * overlap on the GPU. */
+XRGPU_API int xrgpu_mmnb_forward(const xrgpu_mmnb_problem* p, void* workspace, uint64_t workspace_bytes,
+                       void* stream);
+
+/* Enqueues W[n, k] = (float(q) - z) * s as float32 [N, K] (bit-exact nbitWeight,
+ * complex_kernel.glsl:80). Uses p->b, scales, zero_points, K, N, block_size, bits, dtype. */
+XRGPU_API int xrgpu_mmnb_dequantize(const xrgpu_mmnb_problem* p, float* w, void* stream);
+
+/* Name of the kernel path the planner selects for p ("generic", "gemv", "gemm"). */
+XRGPU_API int xrgpu_mmnb_select_path(const xrgpu_mmnb_problem* p, char* name, uint64_t capacity);
+
+/* Reads (and optionally clears) the device error word of `device`: 0 = no error; otherwise a
+ * code (1 = bounded wait expired in a kernel). */
+XRGPU_API int xrgpu_device_error(int32_t device, uint32_t* code, int32_t clear);
+
+/* Library version string. */
+XRGPU_API const char* xrgpu_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XRGPU_MMNB_H */

@@ -1,0 +1,51 @@
+// Internal declarations shared by the host API and the kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace xrgpu {
+
+enum ZpKind : int { kZpNone = 0, kZpF32 = 1, kZpF16 = 2, kZpPacked = 3 };
+enum Path : int { kPathAuto = 0, kPathGeneric = 1, kPathGemv = 2, kPathGemm = 3 };
+
+// A fully validated MatMulNBits problem over device pointers.
+struct Problem {
+  int f16;            // 1: aT/scalesT/biasT/yT are float16, 0: float32
+  int zp;             // ZpKind
+  int64_t M, K, N, bs, bits, kb, blob, ldy;
+  const void* a;
+  const uint8_t* b;
+  const void* scales;
+  const void* zp_ptr;
+  const void* bias;
+  void* y;
+  unsigned* err;      // device error word (see device_error_word())
+};
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+// Generic path: any bits / block size / dtype / zero-point form, float32 accumulation.
+cudaError_t launch_generic(const Problem& p, cudaStream_t s);
+// Exact float32 dequantization W[N, K] (nbitWeight).
+cudaError_t launch_dequant(const Problem& p, float* w, cudaStream_t s);
+
+// 4-bit decode GEMV on mma.sync tensor cores, M <= 16, float16 activations.
+bool gemv_supported(const Problem& p);
+uint64_t gemv_workspace_bytes(const Problem& p);
+cudaError_t launch_gemv(const Problem& p, void* workspace, cudaStream_t s);
+
+// 4-bit prefill GEMM on tcgen05 tensor cores (sm_100a), float16 activations.
+bool gemm_supported(const Problem& p);
+uint64_t gemm_workspace_bytes(const Problem& p);
+cudaError_t launch_gemm(const Problem& p, void* workspace, cudaStream_t s);
+
+// Device error word of the current device (nonzero after a kernel's bounded wait expired).
+unsigned* device_error_word();
+cudaError_t read_device_error(uint32_t* code, bool clear);
+
+}  // namespace xrgpu
