@@ -21,7 +21,7 @@
 // 32). A CTA of 4 warps holds `tpc` column tiles and splits its k range into 4/tpc slices;
 // it stages its activations once (cp.async, permuted in place into mma B-fragment order).
 // Per-block scales and zero points go, 8 regions at a time, into a per-warp window of
-// 8-byte records (float32 scale + float16 unpack constants or float32 zero point), loaded one
+// 16-byte records (float32 scale, float16x2 unpack constants, float32 zero point), loaded one
 // chunk ahead (vectorised when the block size is 32 and K is a multiple of 256). Split-K CTAs
 // of one column group form a thread-block cluster and combine their partial sums in a fixed
 // order through distributed shared memory: no global workspace, deterministic results.
@@ -88,13 +88,12 @@ __device__ __forceinline__ void unpack8(uint32_t w, uint32_t c_lo, uint32_t c_hi
   q[3] = hfma2_u32(lop3_and_or(w8, kHi, kExp), kSixteenth, c_hi);
 }
 
-// float16 unpack constants for an integer zero point z in [0, 15] (4-bit codes), packed as
-// (1024 + z) | (-(64 + z)) << 16: 1024 + z has ulp 1; 64 + z (< 128) has ulp 1/16.
-__host__ __device__ __forceinline__ constexpr uint32_t zconst_packed(uint32_t z) {
-  return (0x6400u + z) | ((0xD400u + (z << 4)) << 16);
+// float16x2 unpack constants for an integer zero point z in [0, 15] (4-bit codes):
+// (1024 + z, 1024 + z) (ulp 1) and (-(64 + z), -(64 + z)) (64 + z < 128 has ulp 1/16).
+__host__ __device__ __forceinline__ constexpr uint32_t zconst_lo(uint32_t z) { return (0x6400u + z) * 0x00010001u; }
+__host__ __device__ __forceinline__ constexpr uint32_t zconst_hi(uint32_t z) {
+  return (0xD400u + (z << 4)) * 0x00010001u;
 }
-__device__ __forceinline__ uint32_t zc_lo(uint32_t packed) { return prmt(packed, packed, 0x1010); }
-__device__ __forceinline__ uint32_t zc_hi(uint32_t packed) { return prmt(packed, packed, 0x3232); }
 
 __device__ __forceinline__ void cp_async_16(uint32_t smem_addr, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gmem) : "memory");
@@ -178,15 +177,16 @@ __device__ __forceinline__ void mma_half(Acc<MT>& acc, uint32_t wa, uint32_t wb,
   }
 }
 
-// y += s * (d - z * sum(x)) with the block records ra (column A) and rb (column B).
+// y += s * (d - z * sum(x)) with the block records ra (column A) and rb (column B):
+// record = {float32 scale, unpack constant lo, unpack constant hi, float32 zero point}.
 template <int MT, int ZM>
-__device__ __forceinline__ void finish_block(Acc<MT>& acc, uint2 ra, uint2 rb) {
+__device__ __forceinline__ void finish_block(Acc<MT>& acc, uint4 ra, uint4 rb) {
   const float sa = __uint_as_float(ra.x), sb = __uint_as_float(rb.x);
 #pragma unroll
   for (int t = 0; t < MT; ++t) {
     float d0 = acc.d[t][0], d1 = acc.d[t][1], d2 = acc.d[t][2], d3 = acc.d[t][3];
     if (ZM == kModeFloat) {
-      const float za = __uint_as_float(ra.y), zb = __uint_as_float(rb.y);
+      const float za = __uint_as_float(ra.w), zb = __uint_as_float(rb.w);
       d0 = fmaf(-za, acc.xs[t][0], d0);
       d1 = fmaf(-za, acc.xs[t][1], d1);
       d2 = fmaf(-zb, acc.xs[t][0], d2);
@@ -200,16 +200,28 @@ __device__ __forceinline__ void finish_block(Acc<MT>& acc, uint2 ra, uint2 rb) {
 }
 
 template <int ZM>
-__device__ __forceinline__ void block_consts(uint2 ra, uint2 rb, uint32_t& clo_a, uint32_t& chi_a, uint32_t& clo_b,
+__device__ __forceinline__ void block_consts(uint4 ra, uint4 rb, uint32_t& clo_a, uint32_t& chi_a, uint32_t& clo_b,
                                              uint32_t& chi_b) {
   if (ZM == kModeInt) {
-    clo_a = zc_lo(ra.y); chi_a = zc_hi(ra.y);
-    clo_b = zc_lo(rb.y); chi_b = zc_hi(rb.y);
+    clo_a = ra.y; chi_a = ra.z;
+    clo_b = rb.y; chi_b = rb.z;
   } else {
-    constexpr uint32_t packed = zconst_packed(ZM == kModeFloat ? 0u : 8u);
-    clo_a = clo_b = (packed & 0xFFFFu) * 0x00010001u;
-    chi_a = chi_b = (packed >> 16) * 0x00010001u;
+    clo_a = clo_b = zconst_lo(ZM == kModeFloat ? 0u : 8u);
+    chi_a = chi_b = zconst_hi(ZM == kModeFloat ? 0u : 8u);
   }
+}
+
+// Stores one 16-byte record (scale, zero point) for the given mode.
+template <int ZM>
+__device__ __forceinline__ void store_record(uint32_t addr, float scale, float z) {
+  uint32_t lo = 0u, hi = 0u;
+  if (ZM == kModeInt) {
+    lo = zconst_lo(static_cast<uint32_t>(z));
+    hi = zconst_hi(static_cast<uint32_t>(z));
+  }
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(__float_as_uint(scale)), "r"(lo), "r"(hi),
+               "r"(__float_as_uint(z))
+               : "memory");
 }
 
 // ----------------------------------------------------------------- metadata chunks
@@ -236,24 +248,23 @@ __device__ __forceinline__ void meta_vec_load(const GemvParams& p, MetaVec& mv, 
 
 template <int ZM>
 __device__ __forceinline__ void meta_vec_store(const MetaVec& mv, uint32_t win_u32, int win_stride, int lane) {
-  const uint32_t base = win_u32 + static_cast<uint32_t>((lane & 15) * win_stride + 8 * (lane >> 4)) * 8u;
+  const uint32_t base = win_u32 + static_cast<uint32_t>((lane & 15) * win_stride + 8 * (lane >> 4)) * 16u;
   const uint32_t sw[4] = {mv.s.x, mv.s.y, mv.s.z, mv.s.w};
   const uint32_t zw[4] = {mv.z.x, mv.z.y, mv.z.z, mv.z.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const __half2 s2 = *reinterpret_cast<const __half2*>(&sw[i]);
-    uint32_t aux0 = 0u, aux1 = 0u;
+    float z0 = 0.f, z1 = 0.f;
     if (ZM == kModeInt) {
-      aux0 = zconst_packed((zw[0] >> (8 * i)) & 15u);
-      aux1 = zconst_packed((zw[0] >> (8 * i + 4)) & 15u);
+      z0 = static_cast<float>((zw[0] >> (8 * i)) & 15u);
+      z1 = static_cast<float>((zw[0] >> (8 * i + 4)) & 15u);
     } else if (ZM == kModeFloat) {
       const __half2 z2 = *reinterpret_cast<const __half2*>(&zw[i]);
-      aux0 = __float_as_uint(__low2float(z2));
-      aux1 = __float_as_uint(__high2float(z2));
+      z0 = __low2float(z2);
+      z1 = __high2float(z2);
     }
-    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(base + 16u * i), "r"(__float_as_uint(__low2float(s2))),
-                 "r"(aux0), "r"(__float_as_uint(__high2float(s2))), "r"(aux1)
-                 : "memory");
+    store_record<ZM>(base + 32u * i, __low2float(s2), z0);
+    store_record<ZM>(base + 32u * i + 16u, __high2float(s2), z1);
   }
 }
 
@@ -292,16 +303,15 @@ __device__ __forceinline__ void meta_scalar_load(const GemvParams& p, MetaScalar
 }
 
 template <int ZM>
-__device__ __forceinline__ void meta_scalar_store(const MetaScalar& mr, uint2* win, int win_stride, int lane,
+__device__ __forceinline__ void meta_scalar_store(const MetaScalar& mr, uint32_t win_u32, int win_stride, int lane,
                                                   int log2_nb) {
   const int nb = 1 << log2_nb;
 #pragma unroll
   for (int i = 0; i < kMetaPerLane; ++i) {
     const int e = lane + 32 * i;
-    if (e < kCols * nb) {
-      const uint32_t aux = ZM == kModeInt ? zconst_packed(static_cast<uint32_t>(mr.z[i])) : __float_as_uint(mr.z[i]);
-      win[(e >> log2_nb) * win_stride + (e & (nb - 1))] = make_uint2(__float_as_uint(mr.s[i]), aux);
-    }
+    if (e < kCols * nb)
+      store_record<ZM>(win_u32 + static_cast<uint32_t>((e >> log2_nb) * win_stride + (e & (nb - 1))) * 16u, mr.s[i],
+                       mr.z[i]);
   }
 }
 
@@ -334,10 +344,14 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const __grid_constant
   const int log2_nb = 31 - __clz(p.nb_chunk);
 
   unsigned char* xs = smem_raw;
-  uint2* win = reinterpret_cast<uint2*>(smem_raw + p.smem_x_bytes) + warp * kCols * p.win_stride;
-  const uint32_t win_u32 = smem_u32(win);
+  const uint32_t win_u32 = smem_u32(smem_raw + p.smem_x_bytes) + static_cast<uint32_t>(warp * kCols * p.win_stride) * 16u;
   const uint32_t ring_u32 =
-      smem_u32(smem_raw + p.smem_x_bytes + kWarps * kCols * p.win_stride * 8) + static_cast<uint32_t>(warp * kRingBytes);
+      smem_u32(smem_raw + p.smem_x_bytes + kWarps * kCols * p.win_stride * 16) + static_cast<uint32_t>(warp * kRingBytes);
+
+  // Programmatic dependent launch: let the next kernel in the stream start its own weight
+  // prefetch while this one runs; everything that may depend on earlier kernels (the
+  // activations read below, the output written at the end) comes after griddepcontrol.wait.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // ---- weight stream: batch j (regions wr0 + 4j ..) goes to stage j % kStages. Lane (g, c)
   // copies 16 bytes of columns A and B for each pair of regions: region 2jj + (c >> 1) of the
@@ -371,6 +385,8 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const __grid_constant
     if (VEC) meta_vec_load<ZM>(p, mv, n0, (wr0 * kRegionK) >> p.log2_bs, lane);
     else meta_scalar_load<ZM>(p, ms, n0, (wr0 * kRegionK) >> p.log2_bs, lane, log2_nb);
   }
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- stage the CTA's activations (cp.async, 16-byte chunks) and permute them in place
   // into mma B-fragment order: (x0,x4), (x2,x6), (x1,x5), (x3,x7).
@@ -408,12 +424,12 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const __grid_constant
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc.y[t][i] = acc.d[t][i] = acc.xs[t][i] = 0.f;
   uint32_t clo_a, chi_a, clo_b, chi_b;
-  block_consts<ZM>(make_uint2(0u, 0u), make_uint2(0u, 0u), clo_a, chi_a, clo_b, chi_b);
+  block_consts<ZM>(make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), clo_a, chi_a, clo_b, chi_b);
   const bool row_ok0 = g < M, row_ok1 = g + 8 < M;
 
   if (tile_ok) {
-    const uint32_t recA0 = win_u32 + static_cast<uint32_t>(g * p.win_stride) * 8u;
-    const uint32_t recB0 = win_u32 + static_cast<uint32_t>((g + 8) * p.win_stride) * 8u;
+    const uint32_t recA0 = win_u32 + static_cast<uint32_t>(g * p.win_stride) * 16u;
+    const uint32_t recB0 = win_u32 + static_cast<uint32_t>((g + 8) * p.win_stride) * 16u;
     const uint32_t xrow8 = static_cast<uint32_t>(8 * p.xrow_bytes);
     const uint32_t xbase = smem_u32(xs) + static_cast<uint32_t>(g * p.xrow_bytes + koff(EXCH, 0, c) * 2);
     constexpr uint32_t kHalfStep = EXCH ? 64u : 16u;  // bytes between the halves' activation chunks
@@ -429,7 +445,7 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const __grid_constant
         // Records of this chunk into the window; the next chunk's metadata goes in flight.
         __syncwarp();
         if (VEC) meta_vec_store<ZM>(mv, win_u32, p.win_stride, lane);
-        else meta_scalar_store<ZM>(ms, win, p.win_stride, lane, log2_nb);
+        else meta_scalar_store<ZM>(ms, win_u32, p.win_stride, lane, log2_nb);
         blk_first = (reg * kRegionK) >> p.log2_bs;
         if (reg + kChunk < wr1) {
           if (VEC) meta_vec_load<ZM>(p, mv, n0, ((reg + kChunk) * kRegionK) >> p.log2_bs, lane);
@@ -448,12 +464,12 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const __grid_constant
         if (r < wr1) {
           const uint32_t xa = xb + u * (kRegionK * 2);
           if (EXCH) {
-            const uint32_t rec = static_cast<uint32_t>(2 * r - blk_first) * 8u;
+            const uint32_t rec = static_cast<uint32_t>(2 * r - blk_first) * 16u;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const uint32_t wa = lds32(rdA + so + 32u * u + 16u * h);
               const uint32_t wb = lds32(rdB + so + 32u * u + 16u * h);
-              const uint2 ma = lds64(recA0 + rec + 8u * h), mb = lds64(recB0 + rec + 8u * h);
+              const uint4 ma = lds128(recA0 + rec + 16u * h), mb = lds128(recB0 + rec + 16u * h);
               block_consts<ZM>(ma, mb, clo_a, chi_a, clo_b, chi_b);
               mma_half<MT, ZM>(acc, wa, wb, clo_a, chi_a, clo_b, chi_b, xa + kHalfStep * h, xrow8, row_ok0, row_ok1, true);
               finish_block<MT, ZM>(acc, ma, mb);
@@ -461,10 +477,10 @@ __global__ void __launch_bounds__(kThreads) gemv_q4_kernel(const __grid_constant
           } else {
             const uint2 wa = lds64(rdA + so + 32u * u), wb = lds64(rdB + so + 32u * u);
             const int gk = r * kRegionK;
-            const uint32_t rec = static_cast<uint32_t>((gk >> p.log2_bs) - blk_first) * 8u;
+            const uint32_t rec = static_cast<uint32_t>((gk >> p.log2_bs) - blk_first) * 16u;
             const bool starts = (gk & bmask) == 0 || (u == 0 && chunk_start);
             const bool ends = ((gk + kRegionK) & bmask) == 0 || r + 1 == cend;
-            const uint2 ma = lds64(recA0 + rec), mb = lds64(recB0 + rec);
+            const uint4 ma = lds128(recA0 + rec), mb = lds128(recB0 + rec);
             if (starts) block_consts<ZM>(ma, mb, clo_a, chi_a, clo_b, chi_b);
             mma_half<MT, ZM>(acc, wa.x, wb.x, clo_a, chi_a, clo_b, chi_b, xa, xrow8, row_ok0, row_ok1, starts);
             mma_half<MT, ZM>(acc, wa.y, wb.y, clo_a, chi_a, clo_b, chi_b, xa + kHalfStep, xrow8, row_ok0, row_ok1, false);
@@ -540,7 +556,8 @@ GemvShape gemv_shape(const Problem& p) {
   s.group_regions = s.vec ? std::max(block_regions, 4) : block_regions;
   s.groups = regions / s.group_regions;
   s.nb_chunk = static_cast<int>(std::max<int64_t>(1, kChunk * kRegionK / p.bs));
-  s.win_stride = s.vec ? s.nb_chunk + 2 : (s.nb_chunk | 1);  // vec: 16-byte aligned rows
+  // 16-byte records; rows of nb + 1 records keep the 8 rows a warp reads in distinct banks.
+  s.win_stride = s.nb_chunk >= 2 ? s.nb_chunk + 1 : 3;
   const int sms = device_sm_count();
   const int target = sms * kTargetWarps;
   s.tpc = s.tiles >= target ? 4 : (s.tiles >= target / 2 ? 2 : 1);
@@ -551,7 +568,7 @@ GemvShape gemv_shape(const Problem& p) {
     const int cta_regions = static_cast<int>(ceil_div(s.groups, splits)) * s.group_regions;
     s.xrow_bytes = cta_regions * kRegionK * 2 + 64;  // +64 B: rows alternate shared-memory bank halves
     s.smem_x_bytes = static_cast<int>(p.M) * s.xrow_bytes;
-    s.smem = static_cast<size_t>(s.smem_x_bytes) + static_cast<size_t>(kWarps) * kCols * s.win_stride * 8 +
+    s.smem = static_cast<size_t>(s.smem_x_bytes) + static_cast<size_t>(kWarps) * kCols * s.win_stride * 16 +
              static_cast<size_t>(kWarps) * kRingBytes;
     if (s.smem <= static_cast<size_t>(kSmemBudget) || splits >= std::min(kMaxSplits, s.groups)) break;
   }
@@ -569,13 +586,15 @@ cudaError_t launch_variant(const GemvShape& s, const GemvParams& gp, cudaStream_
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = s.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = static_cast<unsigned>(s.splits);
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, gp);
 }
 
