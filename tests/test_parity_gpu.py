@@ -160,6 +160,97 @@ def test_gemv_writes_strided_output_slice(F):
     assert within_baseline_tol(out[:, N:2 * N], ref)[0]
 
 
+# ----------------------------------------------------------------- prefill GEMM (tcgen05)
+GEMM_SHAPES = [
+    # (M, K, N, bs): ragged M and N tiles, bs 16..128, one and many K steps, several tiles per CTA
+    (1, 1024, 128, 32), (17, 2048, 100, 64), (64, 1024, 256, 16), (300, 1024, 384, 32),
+    (129, 4096, 200, 128), (2048, 2048, 4096, 64), (520, 4096, 1056, 64), (40, 512, 64, 64),
+]
+
+
+def gemm_geometry_ok(K, bs, zp_kind):
+    """The GEMM's TMA windows need 16-byte rows of scales (ceil(K/bs) % 8 == 0) and, for packed
+    zero points, of zero-point bytes (ceil(K/bs) % 32 == 0); other shapes run the generic kernel."""
+    kb = K // bs
+    return K % 64 == 0 and kb % 8 == 0 and (zp_kind != "packed" or kb % 32 == 0)
+
+
+@pytest.mark.parametrize("M,K,N,bs", GEMM_SHAPES)
+@pytest.mark.parametrize("zp_kind", [None, "float16", "packed"])
+def test_gemm_matches_oracle(F, M, K, N, bs, zp_kind):
+    rng = np.random.default_rng(M * 7 + K + N * 3 + bs)
+    zk = {"float16": np.float16}.get(zp_kind, zp_kind)
+    a, b, s, zp, bias = make(rng, M, K, N, 4, bs, np.float16, zk, bias=(M % 2 == 0))
+    if not gemm_geometry_ok(K, bs, zp_kind):
+        with pytest.raises(ValueError):
+            F.select_path(dev(a), dev(b), dev(s), dev(zp), K=K, N=N, bits=4, block_size=bs, path="gemm")
+        assert F.select_path(dev(a), dev(b), dev(s), dev(zp), K=K, N=N, bits=4, block_size=bs) == (
+            "gemv" if M <= 16 else "generic")
+        return
+    assert F.select_path(dev(a), dev(b), dev(s), dev(zp), K=K, N=N, bits=4, block_size=bs, path="gemm") == "gemm"
+    if M > 16:
+        assert F.select_path(dev(a), dev(b), dev(s), dev(zp), K=K, N=N, bits=4, block_size=bs) == "gemm"
+    y = run_gpu(F, a, b, s, zp, bias, K=K, N=N, bits=4, bs=bs, path="gemm")
+    ref = O.matmul_nbits(a, b, s, zp, bias, K=K, N=N, bits=4, block_size=bs)
+    ok, st = within_baseline_tol(y, ref)
+    assert ok, st
+    # weights rounded once to float16 (the exact float32 weight's nearest float16) before the
+    # float32 tensor-core sum, plus the float16 output rounding
+    err = np.abs(y.astype(np.float64) - ref.astype(np.float64))
+    assert np.all(err <= 4e-3 * np.abs(ref.astype(np.float64)) + 2e-3 * np.abs(ref).max() + 1e-6)
+
+
+def test_gemm_prefill_full_size_properties(F):
+    """Config 4 (M=2048, K=4096, N=14336, bs=64, no zero points) at full size: deterministic,
+    exactly linear in A, and within the tolerance of the oracle on a row x column sample."""
+    rng = np.random.default_rng(4)
+    M, K, N, bs = 2048, 4096, 14336, 64
+    a, b, s, _, _ = make(rng, M, K, N, 4, bs, np.float16, None)
+    da, db, ds = dev(a), dev(b), dev(s)
+    assert F.select_path(da, db, ds, None, K=K, N=N, block_size=bs) == "gemm"
+    y1 = F.matmul_nbits(da, db, ds, None, K=K, N=N, block_size=bs)
+    y2 = F.matmul_nbits(da, db, ds, None, K=K, N=N, block_size=bs)
+    y_2a = F.matmul_nbits(da * 2, db, ds, None, K=K, N=N, block_size=bs)
+    torch.cuda.synchronize()
+    assert F.device_error(0) == 0
+    assert torch.equal(y1, y2)
+    # Exactly linear in A (every product and partial sum doubles), except where y1 was rounded
+    # into the float16 subnormal range, whose absolute grid (2^-24) does not scale.
+    normal = y1.float().abs() >= 2.0 ** -14
+    assert torch.equal(y_2a[normal], (y1 * 2)[normal])
+    assert torch.all((y_2a.float() - 2 * y1.float()).abs()[~normal] <= 2.0 ** -24)
+    rows = np.r_[0:64, M - 64:M]
+    y_host = y1.cpu().numpy()
+    for cs in (slice(0, 256), slice(N - 256, N)):
+        ref = O.matmul_nbits(a[rows], b, s, None, K=K, N=N, bits=4, block_size=bs, columns=cs)
+        ok, st = within_baseline_tol(y_host[rows][:, cs], ref)
+        assert ok, st
+
+
+def test_gemm_writes_strided_output_slice(F):
+    rng = np.random.default_rng(6)
+    M, K, N, bs = 80, 1024, 160, 32
+    a, b, s, zp, bias = make(rng, M, K, N, 4, bs, np.float16, "packed", bias=True)
+    assert F.select_path(dev(a), dev(b), dev(s), dev(zp), K=K, N=N, block_size=bs) == "gemm"
+    big = torch.full((M, 3 * N), 7.0, dtype=torch.float16, device="cuda")
+    F.matmul_nbits(dev(a), dev(b), dev(s), dev(zp), dev(bias), K=K, N=N, block_size=bs, out=big[:, N:2 * N])
+    torch.cuda.synchronize()
+    ref = O.matmul_nbits(a, b, s, zp, bias, K=K, N=N, bits=4, block_size=bs)
+    out = big.cpu().numpy()
+    assert np.all(out[:, :N] == 7.0) and np.all(out[:, 2 * N:] == 7.0)
+    assert within_baseline_tol(out[:, N:2 * N], ref)[0]
+
+
+def test_gemm_unsupported_forms_fall_back_to_generic(F):
+    rng = np.random.default_rng(8)
+    # K not a multiple of 64; float32 activations; 8-bit codes: the planner keeps the generic kernel
+    for (K, dt, bits) in [(96, np.float16, 4), (512, np.float32, 4), (512, np.float16, 8)]:
+        a, b, s, zp, _ = make(rng, 32, K, 64, bits, 32, dt, None)
+        assert F.select_path(dev(a), dev(b), dev(s), None, K=K, N=64, bits=bits, block_size=32) == "generic"
+        with pytest.raises(ValueError):
+            F.select_path(dev(a), dev(b), dev(s), None, K=K, N=64, bits=bits, block_size=32, path="gemm")
+
+
 def test_f16_accumulator_cancellation_gemv(F):
     K, N, bs = 8192, 8, 32
     kb = K // bs

@@ -72,7 +72,8 @@ def build(force: bool = False, verbose_ptxas: bool = False, jobs: int | None = N
     with ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 1)) as pool:
         objects = list(pool.map(one, _sources()))
     tmp = LIBRARY.with_suffix(".so.tmp")
-    cmd = [compiler, "-shared", *ARCH, "-o", str(tmp), *map(str, objects), "-Xcompiler", "-fPIC", "-lcuda"]
+    # No -lcuda: driver entry points (the TMA descriptor encoder) are resolved at run time.
+    cmd = [compiler, "-shared", *ARCH, "-o", str(tmp), *map(str, objects), "-Xcompiler", "-fPIC"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
