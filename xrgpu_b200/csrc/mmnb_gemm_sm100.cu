@@ -4,24 +4,30 @@
 // (nbitWeight / packedMatmul of kernels/_shared/extended/shaders/complex_kernel.glsl:80,83).
 //
 // Orientation. One MMA computes D[n, m] += W[n, k] * A[m, k] for 128 weight rows (the MMA's M)
-// and T activation rows (the MMA's N, 16 <= T <= 256, chosen per problem): the weight tile is
+// and T activation rows (the MMA's N, 16 <= T <= 192, chosen per problem): the weight tile is
 // operand A and lives in tensor memory, the activation tile is operand B in shared memory.
 // Dequantized weights therefore never touch shared memory: the dequantizing warps unpack the
 // TMA-staged nibbles in registers and write float16 straight into TMEM with tcgen05.st. The
 // only shared-memory operand traffic is the activation tile (1/128 byte per flop).
 //
-// Warp roles (18 warps, one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: activation tile [T x 64] (128-byte swizzle, the UMMA K-major
-//               canonical layout), packed nibbles [128 x 32 B], an 8-block window of scales
-//               and of zero points per 64-wide K step, into a ring of `stages` buffers.
-//   warp 1      TMEM allocator and single-thread MMA issuer (4 x tcgen05.mma K=16 per step).
-//   warps 2-9   dequantizers: warp w owns TMEM lane quadrant w % 4 (32 weight rows) and one
-//               32-wide half of the K step; each thread dequantizes one row's 32 codes.
-//   warps 10-17 epilogue: lane quadrant w % 4, half of the T accumulator columns; adds the
+// Warp roles (26 warps, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer (one lane): activation tile [T x 64] (128-byte swizzle, the UMMA
+//               K-major canonical layout), packed nibbles [128 x 32 B], an 8-block window of
+//               scales and of zero points per 64-wide K step, into a ring of `stages` buffers.
+//   warp 1      TMEM allocator and single-lane MMA issuer (4 x tcgen05.mma K=16, one commit
+//               per step).
+//   warps 2-17  dequantizers, four groups of four warps: group j handles the K steps g with
+//               g % 4 == j (each warp has four steps of MMA time per step it dequantizes);
+//               warp w owns TMEM lane quadrant w % 4, one weight row per thread.
+//   warps 18-25 epilogue: lane quadrant w % 4, half of the T accumulator columns; adds the
 //               bias, rounds to float16 and stores Y (masked at the M / N edges).
 //
-// Tensor memory (512 columns, allocated once): columns [0, T) fp32 accumulator, columns
-// [256, 512) eight 32-column stages of dequantized weights (64 float16 per lane each).
+// Tensor memory (512 columns, allocated once): two fp32 accumulator buffers of 192 columns
+// (tile i accumulates in buffer i % 2 while the epilogue drains the other), then four
+// 32-column weight stages (64 float16 per lane each), stage j owned by dequant group j.
+//
+// Only the two issuing lanes poll their mbarriers; the dequant and epilogue warps wait with a
+// hardware-suspending probe so that they take no issue slots from the issuers while idle.
 //
 // Every mbarrier wait is bounded (1 s of device time); on expiry the kernel records an error
 // code in the device error word, raises a CTA-wide abort flag, waits (bounded) for its own
@@ -40,18 +46,22 @@ namespace {
 
 constexpr int kRows = 128;                // weight rows per tile (MMA M)
 constexpr int kStepK = 64;                // K per pipeline step: one 128-byte swizzle row of fp16
-constexpr int kWStages = 8;               // dequantized weight stages in TMEM
-constexpr int kWCols = 32;                // TMEM columns per weight stage
-constexpr int kWCol0 = 256;               // first weight-stage column
-constexpr int kMaxT = 256;                // accumulator columns
+constexpr int kMaxT = 192;                // activation rows per tile (MMA N) at most
+constexpr int kAccCols = kMaxT;           // columns per accumulator buffer (two buffers)
+constexpr int kWStages = 4;               // dequantized weight stages in TMEM
+constexpr int kWCols = 32;                // TMEM columns per weight stage (64 f16 per lane)
+constexpr int kWCol0 = 2 * kAccCols;      // first weight-stage column
 constexpr int kTmemCols = 512;
-constexpr int kDequantWarps = 8;
+static_assert(kWCol0 + kWStages * kWCols == kTmemCols, "TMEM map must fill the 512 columns");
+constexpr int kDqGroups = kWStages;       // dequant group g % 4 owns weight stage g % 4
+constexpr int kDequantWarps = 4 * kDqGroups;
 constexpr int kEpilogueWarps = 8;
 constexpr int kWarps = 2 + kDequantWarps + kEpilogueWarps;
 constexpr int kThreads = kWarps * 32;
 constexpr uint32_t kPackedStage = kRows * 32;  // 64 codes per row per step
 constexpr uint32_t kMetaStage = kRows * 16;    // 16-byte window per row (scales or zero points)
 constexpr int kMaxStages = 8;
+constexpr int kStepOverheadCols = 128;  // per-step fixed cost in MMA columns (tile-height model)
 constexpr int kSmemBudget = 227 * 1024;
 constexpr size_t kOneCtaSmem = 120 * 1024;  // > half of the SM's 228 KB
 
@@ -61,6 +71,7 @@ constexpr unsigned kErrWaitMma = 0x302;
 constexpr unsigned kErrWaitDequant = 0x303;
 constexpr unsigned kErrWaitEpilogue = 0x304;
 constexpr unsigned kErrDrain = 0x305;
+constexpr unsigned kSuspendHintNs = 0x989680;  // longest hardware suspension per mbarrier probe
 
 enum ZpMode : int { kZDefault = 0, kZPacked = 1, kZHalf = 2 };
 
@@ -99,12 +110,14 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                ::"r"(smem_u32(bar)) : "memory");
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-      "%14, %15, %16};"
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
       ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+      "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
@@ -174,12 +187,40 @@ struct Ctl {
   unsigned* err;
 };
 
-// Single-thread bounded wait. Gives up on the abort flag or after the wait limit (raising it).
+// Non-blocking probe of an mbarrier phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// mbarrier probe that may suspend the thread in hardware until the phase completes (or the
+// time hint, in ns, passes).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return done != 0;
+}
+
+// Single-lane bounded spin for the latency-critical roles (TMA producer, MMA issuer).
+// Gives up on the abort flag or after the wait limit (raising it).
 __device__ __forceinline__ bool thread_wait(uint64_t* bar, uint32_t parity, const Ctl& c, unsigned code) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (;;) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test_wait(bar, parity)) return true;
     if (*c.abort) return false;
     if (global_timer_ns() - start > kWaitLimitNs) {
       record_device_error(c.err, code);
@@ -189,13 +230,15 @@ __device__ __forceinline__ bool thread_wait(uint64_t* bar, uint32_t parity, cons
   }
 }
 
-// Whole-warp bounded wait: every lane observes the phase and the warp agrees on the outcome,
-// so the .sync.aligned tcgen05 instructions after it stay converged.
+// Whole-warp bounded wait (dequant and epilogue warps): every lane observes the phase and the
+// warp agrees on the outcome, so the .sync.aligned tcgen05 instructions after it stay
+// converged; the probes suspend the warp in hardware, leaving issue slots to the producer and
+// the MMA issuer. Gives up on the abort flag or after the wait limit (raising it).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const Ctl& c, unsigned code) {
-  if (__all_sync(~0u, mbar_try_wait(bar, parity))) return true;
+  if (__all_sync(~0u, mbar_try_wait_suspend(bar, parity))) return true;
   const uint64_t start = global_timer_ns();
   for (;;) {
-    if (__all_sync(~0u, mbar_try_wait(bar, parity))) return true;
+    if (__all_sync(~0u, mbar_try_wait_suspend(bar, parity))) return true;
     const bool aborted = *c.abort != 0;
     const bool expired = global_timer_ns() - start > kWaitLimitNs;
     if (__any_sync(~0u, aborted || expired)) {
@@ -264,24 +307,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(gbase + bar_off);
   uint64_t* empty = full + S;
   uint64_t* wfull = empty + S;
-  uint64_t* wempty = wfull + kWStages;
-  uint64_t* accfull = wempty + kWStages;
-  uint64_t* accempty = accfull + 1;
-  uint64_t* drain = accempty + 1;
+  uint64_t* accfull = wfull + kWStages;  // [2]
+  uint64_t* accempty = accfull + 2;        // [2]
+  uint64_t* drain = accempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + kDequantWarps);
+      mbar_init(&empty[s], 1 + 4);  // the MMA commit + the 4 warps of the step's dequant group
     }
-    for (int s = 0; s < kWStages; ++s) {
-      mbar_init(&wfull[s], kDequantWarps);
-      mbar_init(&wempty[s], 1);
+    for (int s = 0; s < kWStages; ++s) mbar_init(&wfull[s], 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], kEpilogueWarps);
     }
-    mbar_init(accfull, 1);
-    mbar_init(accempty, kEpilogueWarps);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -301,14 +342,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      int g = 0;
+      int g = 0, s = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < args.tiles; tile += gridDim.x) {
         const int n0 = (tile / args.n_ttiles) * kRows;
         const int m0 = (tile % args.n_ttiles) * args.T;
         for (int ks = 0; ks < ksteps; ++ks, ++g) {
-          const int s = g % S;
-          if (!thread_wait(&empty[s], ((g / S) & 1) ^ 1, ctl, kErrWaitProducer)) {
+          if (!thread_wait(&empty[s], ph ^ 1, ctl, kErrWaitProducer)) {
             ok = false;
             break;
           }
@@ -319,6 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d(sc_s + s * kMetaStage, &map_s, blk & ~7, n0, &full[s]);
           if (ZM == kZPacked) tma_load_2d(zp_s + s * kMetaStage, &map_z, (blk & ~31) >> 1, n0, &full[s]);
           if (ZM == kZHalf) tma_load_2d(zp_s + s * kMetaStage, &map_z, blk & ~7, n0, &full[s]);
+          if (++s == S) {
+            s = 0;
+            ph ^= 1;
+          }
         }
       }
       if (!ok) {
@@ -331,29 +376,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = umma_idesc(args.T);
       const uint64_t desc0 = umma_desc_sw128(tok_s);
-      int g = 0, i = 0;
+      const uint32_t desc_stage = args.tok_stage_bytes >> 4;
+      int i = 0, s = 0, ws = 0;
+      uint32_t wph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < args.tiles; tile += gridDim.x, ++i) {
-        if (!thread_wait(accempty, (i & 1) ^ 1, ctl, kErrWaitMma)) break;
+        const int b = i & 1;  // accumulator buffer: the epilogue drains the other one meanwhile
+        if (!thread_wait(&accempty[b], ((i >> 1) & 1) ^ 1, ctl, kErrWaitMma)) break;
         tc_fence_after();
-        for (int ks = 0; ks < ksteps; ++ks, ++g) {
-          const int s = g % S;
-          const int ws = g % kWStages;
-          if (!thread_wait(&full[s], (g / S) & 1, ctl, kErrWaitMma) ||
-              !thread_wait(&wfull[ws], (g / kWStages) & 1, ctl, kErrWaitMma)) {
+        const uint32_t d_col = tmem + b * kAccCols;
+        for (int ks = 0; ks < ksteps; ++ks) {
+          // wfull of step g implies full[s] of step g: the dequant group read this stage's
+          // nibbles (after the stage's TMA completed) before it arrived.
+          if (!thread_wait(&wfull[ws], wph, ctl, kErrWaitMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t bdesc = desc0 + ((s * args.tok_stage_bytes) >> 4);
+          const uint64_t bdesc = desc0 + s * desc_stage;
           const uint32_t a_col = tmem + kWCol0 + ws * kWCols;
 #pragma unroll
           for (int j = 0; j < kStepK / 16; ++j)
-            mma_ts(tmem, a_col + 8 * j, bdesc + 2 * j, idesc, (ks | j) != 0);
+            mma_ts(d_col, a_col + 8 * j, bdesc + 2 * j, idesc, (ks | j) != 0);
+          // One commit per step: frees input stage s and, for the dequant group of step g + 4,
+          // weight stage ws (both read by exactly these MMAs).
           mma_commit(&empty[s]);
-          mma_commit(&wempty[ws]);
+          if (++s == S) s = 0;
+          if (++ws == kWStages) {
+            ws = 0;
+            wph ^= 1;
+          }
         }
-        if (ok) mma_commit(accfull);
+        if (ok) mma_commit(&accfull[b]);
       }
       // Every MMA this thread issued has completed once `drain` flips.
       mma_commit(drain);
@@ -361,67 +415,83 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < 2 + kDequantWarps) {
     // ------------------------------------------------------------ dequantizers
+    // Group `grp` dequantizes the K steps g = grp, grp + 4, ... into its own TMEM weight stage;
+    // warp w % 4 covers TMEM lanes (weight rows) 32 (w % 4) .. 32 (w % 4) + 31. Step g is K step
+    // g % ksteps of the CTA's tile number g / ksteps, in input stage g % S (S >= 4, so the
+    // stage wraps at most once per advance).
     const int q = warp & 3;
-    const int h = (warp - 2) >> 2;  // which 32-wide half of the K step
-    const int r = 32 * q + lane;    // weight row within the tile
-    const uint32_t lane_addr = static_cast<uint32_t>(32 * q) << 16;
+    const int grp = (warp - 2) >> 2;
+    const int r = 32 * q + lane;  // weight row within the tile
+    const uint32_t w_addr = tmem + (static_cast<uint32_t>(32 * q) << 16) + kWCol0 + grp * kWCols;
     const int bs_log2 = args.bs_log2;
-    int g = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < args.tiles; tile += gridDim.x) {
-      for (int ks = 0; ks < ksteps; ++ks, ++g) {
-        const int s = g % S;
-        const int ws = g % kWStages;
-        if (!warp_wait(&full[s], (g / S) & 1, ctl, kErrWaitDequant)) {
-          ok = false;
-          break;
-        }
-        const uint4 pk = lds128(pk_s + s * kPackedStage + r * 32 + h * 16);
-        // Blocks of this half: b0 (words 0-3), b1 (words 2-3 when bs == 16).
-        const int kfirst = ks * kStepK + h * 32;
-        const int b0 = kfirst >> bs_log2;
-        const int b1 = (kfirst + 16) >> bs_log2;
-        const int w8 = ((ks * kStepK) >> bs_log2) & ~7;
-        const uint32_t srow = sc_s + s * kMetaStage + r * 16;
-        const uint32_t sa = lds_u16(srow + (b0 - w8) * 2);
-        const uint32_t sb = lds_u16(srow + (b1 - w8) * 2);
-        uint32_t adda, addb, za = 0, zb = 0;
+    int tile = blockIdx.x, ks = grp, s = grp;
+    uint32_t ph = 0;
+    int prev_s = -1;  // input stage of this group's previous step g - 4 (none yet)
+    uint32_t prev_ph = 0;
+    while (ks >= ksteps) {
+      ks -= ksteps;
+      tile += gridDim.x;
+    }
+    while (tile < args.tiles) {
+      if (!warp_wait(&full[s], ph, ctl, kErrWaitDequant)) break;
+      const uint32_t prow = pk_s + s * kPackedStage + r * 32;
+      const uint4 p0 = lds128(prow), p1 = lds128(prow + 16);
+      // Word pair j (codes 16j .. 16j+15 of the step) lies in block bj (bs >= 16).
+      const int kbase = ks * kStepK;
+      const int w8 = (kbase >> bs_log2) & ~7;
+      const uint32_t srow = sc_s + s * kMetaStage + r * 16;
+      uint32_t s2[4], add[4], zz[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int bj = (kbase + 16 * j) >> bs_log2;
+        const uint32_t sv = lds_u16(srow + (bj - w8) * 2);
+        s2[j] = sv | (sv << 16);
+        zz[j] = 0;
         if (ZM == kZDefault) {
-          adda = addb = zero_add_pair(8u);
+          add[j] = zero_add_pair(8u);
         } else if (ZM == kZPacked) {
-          const int w32 = ((ks * kStepK) >> bs_log2) & ~31;
-          const uint32_t zrow = zp_s + s * kMetaStage + r * 16;
-          const uint32_t ba = lds_u8(zrow + ((b0 - w32) >> 1));
-          const uint32_t bb = lds_u8(zrow + ((b1 - w32) >> 1));
-          adda = zero_add_pair(((b0 - w32) & 1) ? (ba >> 4) : (ba & 15u));
-          addb = zero_add_pair(((b1 - w32) & 1) ? (bb >> 4) : (bb & 15u));
+          const int w32 = (kbase >> bs_log2) & ~31;
+          const uint32_t zb = lds_u8(zp_s + s * kMetaStage + r * 16 + ((bj - w32) >> 1));
+          add[j] = zero_add_pair(((bj - w32) & 1) ? (zb >> 4) : (zb & 15u));
         } else {
-          const uint32_t zrow = zp_s + s * kMetaStage + r * 16;
-          const uint32_t ha = lds_u16(zrow + (b0 - w8) * 2);
-          const uint32_t hb = lds_u16(zrow + (b1 - w8) * 2);
-          za = ha | (ha << 16);
-          zb = hb | (hb << 16);
-          adda = addb = 0xD400E400u;  // (-1024, -64): exact codes, zero point subtracted after
+          const uint32_t zh = lds_u16(zp_s + s * kMetaStage + r * 16 + (bj - w8) * 2);
+          zz[j] = zh | (zh << 16);
+          add[j] = 0xD400E400u;  // (-1024, -64): exact codes, zero point subtracted after
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done reading stage s
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done reading stage s
 
-        if (!warp_wait(&wempty[ws], ((g / kWStages) & 1) ^ 1, ctl, kErrWaitDequant)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        uint32_t v[16];
-        const uint32_t s2a = sa | (sa << 16), s2b = sb | (sb << 16);
-        dequant_word<ZM>(pk.x, adda, za, s2a, v + 0);
-        dequant_word<ZM>(pk.y, adda, za, s2a, v + 4);
-        dequant_word<ZM>(pk.z, addb, zb, s2b, v + 8);
-        dequant_word<ZM>(pk.w, addb, zb, s2b, v + 12);
-        tmem_st16(tmem + lane_addr + kWCol0 + ws * kWCols + h * 16, v);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&wfull[ws]);
+      // Weight stage `grp` is free once the MMAs of step g - 4 completed: their commit (with
+      // this group's own earlier arrivals) completes the empty phase of that step's stage.
+      if (prev_s >= 0 && !warp_wait(&empty[prev_s], prev_ph, ctl, kErrWaitDequant)) break;
+      tc_fence_after();
+      uint32_t v[32];
+      dequant_word<ZM>(p0.x, add[0], zz[0], s2[0], v + 0);
+      dequant_word<ZM>(p0.y, add[0], zz[0], s2[0], v + 4);
+      dequant_word<ZM>(p0.z, add[1], zz[1], s2[1], v + 8);
+      dequant_word<ZM>(p0.w, add[1], zz[1], s2[1], v + 12);
+      dequant_word<ZM>(p1.x, add[2], zz[2], s2[2], v + 16);
+      dequant_word<ZM>(p1.y, add[2], zz[2], s2[2], v + 20);
+      dequant_word<ZM>(p1.z, add[3], zz[3], s2[3], v + 24);
+      dequant_word<ZM>(p1.w, add[3], zz[3], s2[3], v + 28);
+      tmem_st32(w_addr, v);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wfull[grp]);
+
+      prev_s = s;
+      prev_ph = ph;
+      s += kDqGroups;
+      if (s >= S) {
+        s -= S;
+        ph ^= 1;
+      }
+      ks += kDqGroups;
+      while (ks >= ksteps) {
+        ks -= ksteps;
+        tile += gridDim.x;
       }
     }
   } else {
@@ -434,15 +504,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half_cols = T >> 1;  // multiple of 8
     int i = 0;
     for (int tile = blockIdx.x; tile < args.tiles; tile += gridDim.x, ++i) {
+      const int b = i & 1;
       const int n = (tile / args.n_ttiles) * kRows + 32 * q + lane;
       const int mbase = (tile % args.n_ttiles) * T + c * half_cols;
       const float bias = (args.bias != nullptr && n < args.N) ? __half2float(args.bias[n]) : 0.0f;
-      if (!warp_wait(accfull, i & 1, ctl, kErrWaitEpilogue)) break;
+      if (!warp_wait(&accfull[b], (i >> 1) & 1, ctl, kErrWaitEpilogue)) break;
       tc_fence_after();
       __half* ycol = args.y + n;
       for (int c0 = 0; c0 < half_cols; c0 += 16) {
-        uint32_t va[8], vb[8];
-        const uint32_t taddr = tmem + lane_addr + c * half_cols + c0;
+        uint32_t va[8] = {}, vb[8] = {};
+        const uint32_t taddr = tmem + lane_addr + b * kAccCols + c * half_cols + c0;
         tmem_ld8(taddr, va);
         if (c0 + 8 < half_cols) tmem_ld8(taddr + 8, vb);
         tmem_wait_ld(va, vb);
@@ -459,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(accempty);
+      if (lane == 0) mbar_arrive(&accempty[b]);
     }
   }
 
@@ -483,8 +554,9 @@ int zp_mode(const Problem& p) {
   return p.zp == kZpPacked ? kZPacked : p.zp == kZpF16 ? kZHalf : kZDefault;
 }
 
-// Picks the activation-tile height T (a multiple of 16 up to 256) that minimises the number of
-// persistent rounds times the per-tile cost (T columns of MMA plus a fixed per-tile overhead).
+// Picks the activation-tile height T (a multiple of 16 up to 192) that minimises the number of
+// persistent rounds times the per-tile cost: T columns of MMA per K step plus a fixed per-step
+// cost of the pipeline (synchronisation and MMA issue), measured at about 128 columns' worth.
 GemmShape gemm_shape(const Problem& p, int sms) {
   const int64_t n_w = ceil_div(p.N, kRows);
   GemmShape best{};
@@ -494,7 +566,7 @@ GemmShape gemm_shape(const Problem& p, int sms) {
     const int64_t tiles = n_w * nt;
     if (tiles > INT_MAX) continue;
     const int64_t rounds = ceil_div(tiles, sms);
-    const double cost = static_cast<double>(rounds) * (T + 32);
+    const double cost = static_cast<double>(rounds) * (T + kStepOverheadCols);
     if (best.T == 0 || cost < best_cost || (cost == best_cost && T > best.T)) {
       best.T = T;
       best.n_ttiles = static_cast<int>(nt);
@@ -510,6 +582,7 @@ GemmShape gemm_shape(const Problem& p, int sms) {
   const size_t fixed = 1024 /* alignment slack */ + 512 /* barriers, TMEM slot, abort flag */;
   int stages = static_cast<int>((kSmemBudget - fixed) / stage);
   if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < kDqGroups) stages = 0;  // the dequant groups' stage walk needs S >= 4 (never at T <= 192)
   best.stages = stages;
   best.smem = fixed + static_cast<size_t>(stages) * stage;
   // Each CTA allocates all 512 TMEM columns: request enough shared memory that a second CTA
@@ -583,6 +656,7 @@ cudaError_t launch_gemm(const Problem& p, void*, cudaStream_t stream) {
   if (!gemm_supported(p)) return cudaErrorNotSupported;
   if (p.M == 0) return cudaSuccess;
   const GemmShape sh = gemm_shape(p, device_sm_count());
+  if (sh.stages == 0) return cudaErrorNotSupported;
 
   CUtensorMap ma, mb, msc, mz;
   const uint64_t K = static_cast<uint64_t>(p.K), N = static_cast<uint64_t>(p.N);
