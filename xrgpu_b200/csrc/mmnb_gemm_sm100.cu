@@ -159,11 +159,6 @@ __device__ __forceinline__ uint32_t lds_u8(uint32_t addr) {
   asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
 }
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
 
 // UMMA shared-memory descriptor, K-major operand in the 128-byte swizzle canonical layout:
 // rows of 128 bytes, 8-row atoms 1024 bytes apart (stride byte offset), version 1.
