@@ -105,19 +105,20 @@ struct BlockMeta {
   uint32_t s, z;
 };
 
+// `srow` = col * kb, `zrow` = col * zp_row_bytes (32-bit: N * kb < 2^31 is checked by the planner).
 template <int ZM>
-__device__ __forceinline__ BlockMeta block_meta(const GemvParams& p, int col, int blk) {
+__device__ __forceinline__ BlockMeta block_meta(const GemvParams& p, int srow, int zrow, int blk) {
   BlockMeta m;
-  const int64_t idx = static_cast<int64_t>(col) * p.kb + blk;
-  m.s = __half_as_ushort(p.scales[idx]);
+  const int idx = srow + blk;
+  m.s = __half_as_ushort(__ldg(p.scales + idx));
   m.z = 8u;
   if (ZM == kZPacked) {
-    const uint32_t byte = reinterpret_cast<const uint8_t*>(p.zp)[static_cast<int64_t>(col) * p.zp_row_bytes + (blk >> 1)];
+    const uint32_t byte = __ldg(reinterpret_cast<const uint8_t*>(p.zp) + zrow + (blk >> 1));
     m.z = (byte >> ((blk & 1) * 4)) & 15u;
   }
   if (ZM == kZFloat) {
-    const __half zh = p.zp_f32 ? __float2half_rn(reinterpret_cast<const float*>(p.zp)[idx])
-                               : reinterpret_cast<const __half*>(p.zp)[idx];
+    const __half zh = p.zp_f32 ? __float2half_rn(__ldg(reinterpret_cast<const float*>(p.zp) + idx))
+                               : __ldg(reinterpret_cast<const __half*>(p.zp) + idx);
     m.z = __half_as_ushort(zh);
   }
   return m;
@@ -173,8 +174,10 @@ __device__ __forceinline__ void mma_words(float (&acc)[MT][4], const uint32_t* w
 #pragma unroll
   for (int i = 0; i < NW; ++i) {
     uint4 xv[MT];
-    xv[0] = row0 ? ldg_x128(x0 + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
-    if (MT == 2) xv[MT - 1] = row1 ? ldg_x128(x1 + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+    // Lanes whose activation row is >= M read row 0 instead: B column g only feeds output
+    // row g, which is never stored, so no predication is needed.
+    xv[0] = ldg_x128(x0 + 8 * i);
+    if (MT == 2) xv[MT - 1] = ldg_x128(x1 + 8 * i);
     uint32_t qa[4], qb[4];
     dequant_word<ZM>(wa[i], ca, qa);
     dequant_word<ZM>(wb[i], cb, qb);
@@ -203,9 +206,10 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) gemv_q4_kernel(cons
   const bool do_tail = p.tail && slice == S - 1;
   const bool tile_ok = n0 < p.N;
   const int colA = min(n0 + g, p.N - 1), colB = min(n0 + g + 8, p.N - 1);
-  const int64_t colbytes = static_cast<int64_t>(p.K) / 2;
-  const uint8_t* wA = p.b + colA * colbytes + 16 * c;
-  const uint8_t* wB = p.b + colB * colbytes + 16 * c;
+  // 32-bit offsets (N * K / 2 < 2^31 and N * kb < 2^31 are checked by the planner).
+  const uint8_t* wA = p.b + (colA * (p.K / 2) + 16 * c);
+  const uint8_t* wB = p.b + (colB * (p.K / 2) + 16 * c);
+  const int sA = colA * p.kb, sB = colB * p.kb, zA = colA * p.zp_row_bytes, zB = colB * p.zp_row_bytes;
   const bool row0 = g < p.M, row1 = g + 8 < p.M;
   const __half* xr0 = p.x + static_cast<int64_t>(row0 ? g : 0) * p.K + 32 * c;
   const __half* xr1 = p.x + static_cast<int64_t>(row1 ? g + 8 : 0) * p.K + 32 * c;
@@ -223,44 +227,41 @@ __global__ void __launch_bounds__(kThreads, MT == 1 ? 4 : 3) gemv_q4_kernel(cons
 
   // Block of lane c's codes in iteration it: (128 it + 32 c) / bs.
   auto blk_of = [&](int it) { return (it * kIterK + 32 * c) >> p.log2_bs; };
-  uint4 a_cur = make_uint4(0u, 0u, 0u, 0u), b_cur = a_cur;
-  BlockMeta ma_cur{}, mb_cur{};
-  if (tile_ok && it0 < it1) {
-    a_cur = ldg_w128(wA + it0 * 64);
-    b_cur = ldg_w128(wB + it0 * 64);
-    ma_cur = block_meta<ZM>(p, colA, blk_of(it0));
-    mb_cur = block_meta<ZM>(p, colB, blk_of(it0));
-  }
+  // Two register slots alternate (2-way unrolled loop): the weights of iteration it + 1 are in
+  // flight while iteration it is computed, with no copies between slots.
+  uint4 wa[2], wb[2];
+  BlockMeta ma[2], mb[2];
+  auto fetch = [&](int it, int slot) {
+    wa[slot] = ldg_w128(wA + it * 64);
+    wb[slot] = ldg_w128(wB + it * 64);
+    const int blk = blk_of(it);
+    ma[slot] = block_meta<ZM>(p, sA, zA, blk);
+    mb[slot] = block_meta<ZM>(p, sB, zB, blk);
+  };
+  if (tile_ok && it0 < it1) fetch(it0, 0);
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (tile_ok) {
-    for (int it = it0; it < it1; ++it) {
-      uint4 a_nxt = a_cur, b_nxt = b_cur;
-      BlockMeta ma_nxt = ma_cur, mb_nxt = mb_cur;
-      if (it + 1 < it1) {
-        a_nxt = ldg_w128(wA + (it + 1) * 64);
-        b_nxt = ldg_w128(wB + (it + 1) * 64);
-        const int bn = blk_of(it + 1);
-        if (bn != blk_of(it)) {
-          ma_nxt = block_meta<ZM>(p, colA, bn);
-          mb_nxt = block_meta<ZM>(p, colB, bn);
-        }
-      }
-      const uint32_t wa[4] = {a_cur.x, a_cur.y, a_cur.z, a_cur.w};
-      const uint32_t wb[4] = {b_cur.x, b_cur.y, b_cur.z, b_cur.w};
-      mma_words<MT, ZM, 4>(acc, wa, wb, ma_cur, mb_cur, xr0 + it * kIterK, xr1 + it * kIterK, row0, row1);
-      a_cur = a_nxt;
-      b_cur = b_nxt;
-      ma_cur = ma_nxt;
-      mb_cur = mb_nxt;
+    auto compute = [&](int it, int slot) {
+      const uint32_t a[4] = {wa[slot].x, wa[slot].y, wa[slot].z, wa[slot].w};
+      const uint32_t b[4] = {wb[slot].x, wb[slot].y, wb[slot].z, wb[slot].w};
+      mma_words<MT, ZM, 4>(acc, a, b, ma[slot], mb[slot], xr0 + it * kIterK, xr1 + it * kIterK, row0, row1);
+    };
+    int it = it0;
+    for (; it + 2 <= it1; it += 2) {
+      fetch(it + 1, 1);
+      compute(it, 0);
+      if (it + 2 < it1) fetch(it + 2, 0);
+      compute(it + 1, 1);
     }
+    if (it < it1) compute(it, 0);
     if (do_tail) {
       // Final 64-wide region: lane c holds 8 bytes per column, codes [16c, 16c+16) of it.
       const int kr = p.iters * kIterK;
       const uint2 a2 = ldg_w64(wA - 16 * c + kr / 2 + 8 * c);
       const uint2 b2 = ldg_w64(wB - 16 * c + kr / 2 + 8 * c);
       const int blk = (kr + 16 * c) >> p.log2_bs;
-      const BlockMeta ma = block_meta<ZM>(p, colA, blk), mb = block_meta<ZM>(p, colB, blk);
+      const BlockMeta ma = block_meta<ZM>(p, sA, zA, blk), mb = block_meta<ZM>(p, sB, zB, blk);
       const uint32_t wa[2] = {a2.x, a2.y}, wb[2] = {b2.x, b2.y};
       mma_words<MT, ZM, 2>(acc, wa, wb, ma, mb, xr0 - 32 * c + kr + 16 * c, xr1 - 32 * c + kr + 16 * c, row0, row1);
     }
@@ -350,7 +351,7 @@ cudaError_t launch_variant(const GemvShape& s, const GemvParams& gp, cudaStream_
 
 bool gemv_supported(const Problem& p) {
   return p.f16 && p.bits == 4 && p.M >= 1 && p.M <= 16 && p.bs >= 32 && (p.bs & (p.bs - 1)) == 0 &&
-         p.K % 64 == 0 && p.K % p.bs == 0 && p.K < (1ll << 30) && p.N < (1ll << 30) &&
+         p.K % 64 == 0 && p.K % p.bs == 0 && p.N * (p.K / 2) < (1ll << 31) && p.N * p.kb < (1ll << 31) &&
          (reinterpret_cast<uintptr_t>(p.b) % 16) == 0 && (reinterpret_cast<uintptr_t>(p.a) % 16) == 0 &&
          (reinterpret_cast<uintptr_t>(p.scales) % 2) == 0;
 }
