@@ -1,0 +1,134 @@
+"""N-column sharding with one all-gather of Y.
+
+Host logic (shard bounds, slicing, gather and reassembly) runs as world-size-2 gloo ranks on CPU
+with the oracle as the per-shard compute; the NCCL path runs the CUDA kernels on 2 GPUs when the
+machine has them.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import mmnb_oracle as O
+from xrgpu_b200.sharded import ShardedMatMulNBits, shard_bounds, shard_tensor
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("N", [1, 7, 8, 100, 4096, 14336])
+def test_shard_bounds_cover_columns_once(world, N):
+    seen = []
+    S = -(-N // world)
+    for r in range(world):
+        n0, n1 = shard_bounds(N, world, r)
+        assert 0 <= n0 <= n1 <= N and n1 - n0 <= S
+        seen.extend(range(n0, n1))
+    assert seen == list(range(N))
+
+
+def test_shard_bounds_rejects_bad_rank():
+    with pytest.raises(ValueError):
+        shard_bounds(16, 2, 2)
+
+
+def _case(seed, M, K, N, bs, zp_kind, bias):
+    rng = np.random.default_rng(seed)
+    kb = K // bs
+    a = rng.standard_normal((M, K)).astype(np.float16)
+    b = rng.integers(0, 256, (N, kb, bs // 2), dtype=np.uint8)
+    s = rng.uniform(0.005, 0.02, (N, kb)).astype(np.float16)
+    zp = rng.integers(0, 256, (N, (kb + 1) // 2), dtype=np.uint8) if zp_kind == "packed" else None
+    bb = rng.standard_normal(N).astype(np.float16) if bias else None
+    return a, b, s, zp, bb
+
+
+def _oracle_compute(a, b, scales, zero_points, bias, *, K, N, bits, block_size, out):
+    npy = lambda t: None if t is None else t.numpy()  # noqa: E731
+    y = O.matmul_nbits(npy(a), npy(b), npy(scales), npy(zero_points), npy(bias), K=K, N=N, bits=bits,
+                       block_size=block_size)
+    out.copy_(torch.from_numpy(y))
+    return out
+
+
+CASES = [(1, 256, 37, 32, "packed", True), (3, 128, 64, 64, None, False), (5, 512, 9, 128, "packed", False)]
+
+
+def _gloo_rank(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        for i, (M, K, N, bs, zk, bias) in enumerate(CASES):
+            a, b, s, zp, bb = _case(i, M, K, N, bs, zk, bias)
+            t = lambda x: None if x is None else torch.from_numpy(x)  # noqa: E731
+            mod = ShardedMatMulNBits(t(b), t(s), t(zp), t(bb), K=K, N=N, block_size=bs, compute=_oracle_compute)
+            y = mod(torch.from_numpy(a))
+            # the same module built from this rank's shards alone
+            mod2 = ShardedMatMulNBits.from_shard(shard_tensor(t(b), N, world, rank), shard_tensor(t(s), N, world, rank),
+                                                 shard_tensor(t(zp), N, world, rank), shard_tensor(t(bb), N, world, rank),
+                                                 K=K, N=N, block_size=bs, compute=_oracle_compute)
+            y2 = mod2(torch.from_numpy(a))
+            ref = O.matmul_nbits(a, b, s, zp, bb, K=K, N=N, bits=4, block_size=bs)
+            results[(rank, i)] = (bool(np.array_equal(y.numpy(), ref)), bool(torch.equal(y, y2)), tuple(y.shape))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gloo_ranks_reassemble_the_full_output(world):
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_gloo_rank, args=(world, _free_port(), results), nprocs=world, start_method="spawn")
+    for r in range(world):
+        for i, (M, K, N, *_rest) in enumerate(CASES):
+            exact, same, shape = results[(r, i)]
+            assert exact, (r, i)          # the gathered Y equals the oracle's full Y bit for bit
+            assert same, (r, i)           # full-tensor and from_shard construction agree
+            assert shape == (M, N)
+
+
+def test_single_process_is_a_plain_call():
+    a, b, s, zp, bb = _case(7, 2, 128, 40, 32, "packed", True)
+    t = lambda x: None if x is None else torch.from_numpy(x)  # noqa: E731
+    mod = ShardedMatMulNBits(t(b), t(s), t(zp), t(bb), K=128, N=40, block_size=32, compute=_oracle_compute)
+    y = mod(torch.from_numpy(a))
+    assert np.array_equal(y.numpy(), O.matmul_nbits(a, b, s, zp, bb, K=128, N=40, bits=4, block_size=32))
+
+
+# ----------------------------------------------------------------- NCCL on 2 GPUs
+def _nccl_rank(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from xrgpu_b200 import functional as F
+        for i, (M, K, N, bs) in enumerate([(1, 4096, 4100, 32), (4, 4096, 1024, 128), (64, 1024, 1000, 64)]):
+            a, b, s, zp, bb = _case(100 + i, M, K, N, bs, "packed", True)
+            d = lambda x: None if x is None else torch.from_numpy(x).cuda()  # noqa: E731
+            y = ShardedMatMulNBits(d(b), d(s), d(zp), d(bb), K=K, N=N, block_size=bs)(d(a))
+            y_one = F.matmul_nbits(d(a), d(b), d(s), d(zp), d(bb), K=K, N=N, block_size=bs)
+            torch.cuda.synchronize()
+            # different per-call shapes may split K differently: compare within the tolerance
+            d_max = (y.float() - y_one.float()).abs().max().item()
+            scale = y_one.float().abs().max().item()
+            results[(rank, i)] = bool(y.shape == y_one.shape and d_max <= 2e-3 * scale)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_nccl_two_gpus_match_one_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_nccl_rank, args=(2, _free_port(), results), nprocs=2, start_method="spawn")
+    assert all(results[(r, i)] for r in range(2) for i in range(3)), dict(results)

@@ -1,0 +1,124 @@
+"""N-column sharding of MatMulNBits over the GPUs of one node, with one all-gather of Y.
+
+Every output column of Y = A . dequant(B)^T depends only on its own row of B, scales, zero
+points and bias, all of which are N-major: rank r of a ``torch.distributed`` group owns the
+contiguous column range ``shard_bounds(N, world, r)`` and the matching contiguous slices of those
+tensors, computes its columns of Y with this package's kernels (A is replicated), and one
+all-gather (NCCL over NVLink/NVSwitch) assembles Y. The reference backend is single-device;
+the contract (inputs, attributes, output shape and values) is unchanged.
+
+Shards are equal (``ceil(N / world)`` columns, the last one padded) so that the gather is one
+``all_gather_into_tensor``; for M == 1 the gathered buffer already is Y, for M > 1 one permute
+copy turns ``[world, M, S]`` into ``[M, world * S]``.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import functional as F
+
+__all__ = ["shard_bounds", "shard_tensor", "ShardedMatMulNBits"]
+
+
+def shard_bounds(N: int, world: int, rank: int) -> tuple[int, int]:
+    """Columns [n0, n1) owned by `rank`: equal shards of ceil(N / world) columns (the last ones
+    may be short or empty)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside a group of {world}")
+    S = -(-N // world)
+    n0 = min(N, rank * S)
+    return n0, min(N, n0 + S)
+
+
+def shard_tensor(t: Optional[torch.Tensor], N: int, world: int, rank: int) -> Optional[torch.Tensor]:
+    """This rank's contiguous slice of an N-major tensor (B, scales, zero points, bias)."""
+    if t is None:
+        return None
+    if t.shape[0] != N:
+        raise ValueError(f"expected an N-major tensor with {N} rows, got shape {tuple(t.shape)}")
+    n0, n1 = shard_bounds(N, world, rank)
+    return t[n0:n1].contiguous()
+
+
+class ShardedMatMulNBits:
+    """MatMulNBits with B split by output column across the ranks of a process group.
+
+    Construct with the full tensors (each rank keeps only its slice) or with this rank's shard
+    (``from_shard``); ``forward(a)`` returns the full Y [*, N] on every rank. ``compute`` replaces
+    the per-shard kernel call (default ``functional.matmul_nbits``); its signature is that of
+    ``matmul_nbits`` with ``out`` given.
+    """
+
+    def __init__(self, b: torch.Tensor, scales: torch.Tensor, zero_points: Optional[torch.Tensor] = None,
+                 bias: Optional[torch.Tensor] = None, *, K: int, N: int, bits: int = 4, block_size: int,
+                 group=None, compute: Optional[Callable] = None, _presharded: bool = False):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.K, self.N, self.bits, self.block_size = int(K), int(N), int(bits), int(block_size)
+        self.n0, self.n1 = shard_bounds(self.N, self.world, self.rank)
+        self.S = -(-self.N // self.world)
+        if _presharded:
+            self.b, self.scales, self.zero_points, self.bias = b, scales, zero_points, bias
+        else:
+            self.b = shard_tensor(b, self.N, self.world, self.rank)
+            self.scales = shard_tensor(scales, self.N, self.world, self.rank)
+            self.zero_points = shard_tensor(zero_points, self.N, self.world, self.rank)
+            self.bias = shard_tensor(bias, self.N, self.world, self.rank)
+        if self.b.shape[0] != self.n1 - self.n0:
+            raise ValueError(f"rank {self.rank} shard has {self.b.shape[0]} columns, expected {self.n1 - self.n0}")
+        self.compute = compute or F.matmul_nbits
+
+    @classmethod
+    def from_shard(cls, b_shard: torch.Tensor, scales_shard: torch.Tensor, zero_points_shard=None, bias_shard=None,
+                   *, K: int, N: int, bits: int = 4, block_size: int, group=None, compute=None):
+        """Build from this rank's slices (rows shard_bounds(N, world, rank) of each tensor)."""
+        return cls(b_shard, scales_shard, zero_points_shard, bias_shard, K=K, N=N, bits=bits,
+                   block_size=block_size, group=group, compute=compute, _presharded=True)
+
+    def local(self, a: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """This rank's columns of Y into out[..., :n1 - n0] (out is [M, S], S >= n1 - n0)."""
+        n_local = self.n1 - self.n0
+        if n_local > 0:
+            self.compute(a, self.b, self.scales, self.zero_points, self.bias, K=self.K, N=n_local,
+                         bits=self.bits, block_size=self.block_size, out=out[:, :n_local])
+        if n_local < self.S:
+            out[:, n_local:].zero_()
+        return out
+
+    def forward(self, a: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Full Y [*, N] on every rank. `out` (contiguous, Y's shape) receives it without an extra
+        copy when M == 1 and N is a multiple of the group size."""
+        lead = tuple(a.shape[:-1])
+        M = a.numel() // self.K
+        a2 = a.reshape(M, self.K)
+        y_local = torch.empty((M, self.S), dtype=a.dtype, device=a.device)
+        self.local(a2, y_local)
+        if self.world == 1:
+            y = y_local[:, :self.N]
+            if out is not None:
+                out.view(M, self.N).copy_(y)
+                return out
+            return y.reshape(*lead, self.N)
+        direct = out is not None and M == 1 and self.world * self.S == self.N and out.is_contiguous()
+        gathered = (out.view(self.world, 1, self.S) if direct
+                    else torch.empty((self.world, M, self.S), dtype=a.dtype, device=a.device))
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(gathered, y_local, group=self.group)
+        else:  # gloo (host tests): list form
+            dist.all_gather(list(gathered.unbind(0)), y_local, group=self.group)
+        if direct:
+            return out
+        if M == 1:
+            y = gathered.view(1, self.world * self.S)[:, :self.N]
+        else:
+            y = gathered.permute(1, 0, 2).reshape(M, self.world * self.S)[:, :self.N]
+        if out is not None:
+            out.view(M, self.N).copy_(y)
+            return out
+        return y.reshape(*lead, self.N)
+
+    __call__ = forward
