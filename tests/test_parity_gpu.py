@@ -147,6 +147,23 @@ def test_gemv_deterministic_and_linear_full_size(F):
         assert ok, (K, N, st)
 
 
+def test_gemv_caller_workspace_reused_across_calls(F):
+    """Shared tiles meet in the workspace and each call leaves its counters at zero: repeated calls
+    on one caller-owned workspace give identical results."""
+    rng = np.random.default_rng(21)
+    for (M, K, N, bs) in [(1, 4096, 4096, 32), (3, 14336, 1000, 64), (1, 576, 70, 32)]:
+        a, b, s, zp, bias = make(rng, M, K, N, 4, bs, np.float16, "packed", bias=True)
+        need = F.workspace_size(M, K=K, N=N, bits=4, block_size=bs)
+        ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
+        ys = [F.matmul_nbits(dev(a), dev(b), dev(s), dev(zp), dev(bias), K=K, N=N, block_size=bs, workspace=ws)
+              for _ in range(3)]
+        torch.cuda.synchronize()
+        assert F.device_error(0) == 0
+        assert torch.equal(ys[0], ys[1]) and torch.equal(ys[1], ys[2])
+        ref = O.matmul_nbits(a, b, s, zp, bias, K=K, N=N, bits=4, block_size=bs)
+        assert within_baseline_tol(ys[0].cpu().numpy(), ref)[0]
+
+
 def test_gemv_writes_strided_output_slice(F):
     rng = np.random.default_rng(5)
     M, K, N, bs = 3, 1024, 96, 32

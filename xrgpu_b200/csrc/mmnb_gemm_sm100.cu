@@ -631,6 +631,13 @@ cudaError_t launch_mode(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
 
 }  // namespace
 
+bool encode_tensor_map_2d(void* map, int dtype, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                          uint32_t box_inner, uint32_t box_outer, bool swizzle_128b) {
+  return encode_2d(static_cast<CUtensorMap*>(map), dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                   ptr, inner, outer, row_bytes, box_inner, box_outer,
+                   swizzle_128b ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 bool gemm_supported(const Problem& p) {
   if (!p.f16 || p.bits != 4 || p.M < 1 || p.N < 1) return false;
   if (p.K < kStepK || p.K % kStepK != 0 || p.K > (int64_t(1) << 30)) return false;

@@ -44,6 +44,11 @@ bool gemm_supported(const Problem& p);
 uint64_t gemm_workspace_bytes(const Problem& p);
 cudaError_t launch_gemm(const Problem& p, void* workspace, cudaStream_t s);
 
+// Encodes a 2-D TMA tensor map into `map` (a CUtensorMap, 64-byte aligned, 128 bytes) through the
+// driver entry point resolved at run time. dtype: 0 = uint8, 1 = float16. Returns false on failure.
+bool encode_tensor_map_2d(void* map, int dtype, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                          uint32_t box_inner, uint32_t box_outer, bool swizzle_128b);
+
 // Device error word of the current device (nonzero after a kernel's bounded wait expired).
 unsigned* device_error_word();
 cudaError_t read_device_error(uint32_t* code, bool clear);
