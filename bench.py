@@ -242,8 +242,9 @@ def run_ours(args, wl):
     for layer in range(layers):
         step(layer)
     torch.cuda.synchronize()
-    # Each layer's step is one CUDA graph on one GPU; with N > 1 ranks the step (kernels plus NCCL
-    # all-gathers) is launched eagerly.
+    # Each layer's step is one CUDA graph on one GPU. With N > 1 ranks the step (kernels plus NCCL
+    # all-gathers) is launched eagerly: steps captured with their all-gathers ran, but the end-to-end
+    # section after them stalled.
     use_graphs = world == 1 and not args.no_graphs
     graphs = []
     if use_graphs:
@@ -264,7 +265,9 @@ def run_ours(args, wl):
             else:
                 step(layer)
 
+    log(f"[rank {rank}] graphs captured: {len(graphs)}")
     run_steps(max(3, args.warmup))
+    log(f"[rank {rank}] warm-up done")
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     barrier(world)
@@ -304,7 +307,9 @@ def run_ours(args, wl):
     # Each projection's kernel alone: a CUDA graph of back-to-back launches over the rotating
     # weight copies (no host launch overhead between them).
     kernel = {}
-    if rank == 0 or world == 1:
+    # Per-projection kernel times: one GPU only (no collectives inside; with several ranks one
+    # rank capturing graphs while the others sit in collectives would only add waiting).
+    if world == 1:
         for (name, K, N) in wl["proj"]:
             reps = 4 * layers
             gs = torch.cuda.Stream(device)
@@ -348,6 +353,7 @@ def run_ours(args, wl):
             roofline["traffic"] = tr.get("bytes_per_step")
             roofline["traffic_source"] = tr.get("source")
 
+    log(f"[rank {rank}] timed region done")
     # End to end through the public C-ABI call: pinned host A -> device, the step's C-ABI calls,
     # device -> pinned host Y, synchronise; every step.
     e2e = None
@@ -381,7 +387,8 @@ def run_ours(args, wl):
         e_ms = max_over_ranks(world, max(e0.elapsed_time(e1), wall * 1e3) / args.steps)
         e_val = (bytes_rank * world / (e_ms * 1e-3) / 1e9) if wl["kind"] == "decode" else (flops_rank * world / (e_ms * 1e-3) / 1e12)
         e2e = dict(value=round(e_val, 2), unit=unit, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h, ms_per_step=round(e_ms, 4),
-                   path="functional.matmul_nbits -> xrgpu_mmnb_forward (C ABI), one sync per step")
+                   path=("ShardedMatMulNBits -> " if world > 1 else "") +
+                   "functional.matmul_nbits -> xrgpu_mmnb_forward (C ABI), one sync per step")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
