@@ -140,7 +140,8 @@ def test_gemv_deterministic_and_linear_full_size(F):
         y_2a = F.matmul_nbits(da * 2, db, ds, dz, K=K, N=N, block_size=32)
         torch.cuda.synchronize()
         assert torch.equal(y1, y2)                     # fixed-order split-K reduction
-        assert torch.equal(y_2a, y1 * 2)               # exact: every product doubles
+        normal = y1.abs() >= 2.0 ** -14                # doubling is exact except float16 subnormals
+        assert torch.equal(y_2a[normal], (y1 * 2)[normal])
         cols = slice(0, 512)                           # oracle on a column sample
         ref = O.matmul_nbits(a, b, s, zp, K=K, N=N, bits=4, block_size=32, columns=cols)
         ok, st = within_baseline_tol(y1.cpu().numpy()[:, cols], ref)
