@@ -41,6 +41,9 @@ cudaError_t launch_gemv(const Problem& p, void* workspace, cudaStream_t s);
 // Its single-row (M == 1) form: scale and zero point applied after the MMA.
 bool gemv_m1_supported(const Problem& p);
 cudaError_t launch_gemv_m1(const Problem& p, cudaStream_t s);
+// Its single-row form with the weights staged through shared memory by asynchronous copies.
+bool gemv_staged_supported(const Problem& p);
+cudaError_t launch_gemv_staged(const Problem& p, cudaStream_t s);
 
 // 4-bit prefill GEMM on tcgen05 tensor cores (sm_100a), float16 activations.
 bool gemm_supported(const Problem& p);
