@@ -16,7 +16,9 @@ so every step streams its weights from HBM (config: "l2": "rotating weight copie
 
 Multi-GPU (torchrun, one process per GPU, NCCL): every rank owns a contiguous 1/N slice of each
 projection's output columns (weak scaling: the model is N times wider, per-GPU work fixed) and the
-step ends with one NCCL all-gather of Y per projection. Time is the max over ranks.
+step ends with one all-gather of Y per projection: the library's peer-memory all-gather over NVLink
+for decode shards (the whole step is then one CUDA graph), NCCL for large prefill shards. Time is
+the max over ranks.
 
 --impl reference times the reference's own CPU algorithm (oracle/_ref: packedMatmul/nbitWeight
 compiled from the reference sources; the C oracle port when that is absent) on all host threads,
@@ -221,14 +223,23 @@ def run_ours(args, wl):
     paths = sorted({F.select_path(acts[p["K"]], p["b"], p["s"], p["zp"], K=p["K"], N=p["N"], block_size=wl["bs"])
                     for p in weights[0]})
 
+    shared = None
     if world > 1:
         # Each rank's shard is one column slice of an (N * world)-wide projection, used through the
-        # library's sharded module: local kernel + one NCCL all-gather of Y per projection.
+        # library's sharded module: local kernel + one all-gather of Y per projection (peer memory
+        # for small shards, NCCL otherwise).
         from xrgpu_b200.sharded import ShardedMatMulNBits
+        from xrgpu_b200.p2p import PeerAllGather
         for layer in weights:
             for p in layer:
                 p["mod"] = ShardedMatMulNBits.from_shard(p["b"], p["s"], p["zp"], None, K=p["K"], N=p["N"] * world,
                                                          block_size=wl["bs"])
+        if all(p["mod"].uses_peer_gather(M) for layer in weights for p in layer):
+            # one peer-memory group shared by every projection (calls are stream-ordered)
+            shared = PeerAllGather(max(M * p["N"] * 2 for p in weights[0]))
+            for layer in weights:
+                for p in layer:
+                    p["mod"].set_peer_group(shared)
 
     def step(layer, gather=True):
         for p in weights[layer]:
@@ -242,10 +253,11 @@ def run_ours(args, wl):
     for layer in range(layers):
         step(layer)
     torch.cuda.synchronize()
-    # Each layer's step is one CUDA graph on one GPU. With N > 1 ranks the step (kernels plus NCCL
-    # all-gathers) is launched eagerly: steps captured with their all-gathers ran, but the end-to-end
-    # section after them stalled.
-    use_graphs = world == 1 and not args.no_graphs
+    # Each layer's step is one CUDA graph when it contains no NCCL call: always on one GPU, and with
+    # N > 1 ranks when every projection's all-gather goes through peer memory. Steps that hold NCCL
+    # all-gathers run eagerly.
+    peer = world > 1 and all(p["mod"].uses_peer_gather(M) for layer in weights for p in layer)
+    use_graphs = (world == 1 or peer) and not args.no_graphs
     graphs = []
     if use_graphs:
         stream = torch.cuda.Stream(device)
@@ -396,8 +408,13 @@ def run_ours(args, wl):
 
     if world > 1:
         import torch.distributed as dist
-        graphs.clear()  # graphs holding NCCL calls are released before the process group goes
+        graphs.clear()  # graphs are released before the process group goes
         torch.cuda.synchronize()
+        for layer in weights:
+            for p in layer:
+                p["mod"].close()
+        if shared is not None:
+            shared.close()  # collective: every rank closes it at the same point
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -411,7 +428,8 @@ def run_ours(args, wl):
                    "projections": [[n, K, N] for (n, K, N) in wl["proj"]], "bits": 4, "block_size": wl["bs"],
                    "zero_points": "packed uint8" if wl["zp"] else "none", "l2": f"{layers} rotating weight copies "
                    f"({layers * per_layer / 1e6:.0f} MB > 3x L2)", "parallelism": f"column-shard x{world}" +
-                   (" + NCCL all-gather of Y" if world > 1 else ""), "cuda_graphs": use_graphs, "paths": paths},
+                   ((" + peer-memory all-gather of Y" if peer else " + NCCL all-gather of Y") if world > 1 else ""),
+                   "cuda_graphs": use_graphs, "paths": paths},
         "roofline": roofline, "kernels_us": kernel, "gpu_launches": launches_per_step * args.steps,
         "clocks": clock, "e2e": e2e, "cpu_baseline": cpu,
     }

@@ -208,6 +208,35 @@ XRGPU_API int xrgpu_mmnb_select_path(const xrgpu_mmnb_problem* p, char* name, ui
  * code (1 = bounded wait expired in a kernel). */
 XRGPU_API int xrgpu_device_error(int32_t device, uint32_t* code, int32_t clear);
 
+/* ---- Peer-memory all-gather for column-sharded MatMulNBits (no counterpart in the reference,
+ * whose backend is single-device). One process per GPU on one node; every rank of a group makes
+ * the same sequence of calls. The all-gather is one kernel, so CUDA graphs can capture it. */
+#define XRGPU_P2P_MAX_WORLD 16
+#define XRGPU_P2P_HANDLE_BYTES 64
+typedef struct xrgpu_p2p xrgpu_p2p;
+
+/* Allocates this rank's staging region on `device` (2 * world * slot_bytes + 256 bytes, zero-filled)
+ * and writes its 64-byte CUDA IPC handle to ipc_handle. slot_bytes: largest shard in bytes (a
+ * multiple of 16). */
+XRGPU_API int xrgpu_p2p_create(int32_t device, int32_t world, int32_t rank, uint64_t slot_bytes, xrgpu_p2p** group,
+                               void* ipc_handle);
+
+/* Maps the other ranks' regions: ipc_handles holds world handles of 64 bytes in rank order (this
+ * rank's own entry is ignored). */
+XRGPU_API int xrgpu_p2p_connect(xrgpu_p2p* group, const void* ipc_handles);
+
+/* Enqueues on `stream`: out[m, q * shard_row_bytes + j] = shard of rank q [m, j] for every rank q,
+ * m < rows, keeping the first out_valid_bytes of each output row (the last shard may be padded).
+ * shard is this rank's [rows, shard_row_bytes] (contiguous); shard_row_bytes is a multiple of 16, and
+ * so is out_row_bytes when rows > 1; rows * shard_row_bytes <= slot_bytes. A peer that does not arrive within 1 s
+ * leaves code 0x401 in the device error word (xrgpu_device_error). */
+XRGPU_API int xrgpu_p2p_allgather(xrgpu_p2p* group, const void* shard, int64_t rows, int64_t shard_row_bytes,
+                                  void* out, int64_t out_row_bytes, int64_t out_valid_bytes, void* stream);
+
+/* Unmaps the peers' regions and frees this rank's. Call only after every rank has finished its
+ * last all-gather on the group (synchronise, then a host barrier). */
+XRGPU_API int xrgpu_p2p_destroy(xrgpu_p2p* group);
+
 /* Library version string. */
 XRGPU_API const char* xrgpu_version(void);
 

@@ -24,7 +24,10 @@ EXPORTED = (
     "xrgpu_read_outputs", "xrgpu_info", "xrgpu_close", "xrgpu_destroy", "xrgpu_write_input", "xrgpu_run_async",
     "xrgpu_sync", "xrgpu_output_device_ptr", "xrgpu_mmnb_workspace_size", "xrgpu_mmnb_forward",
     "xrgpu_mmnb_dequantize", "xrgpu_mmnb_select_path", "xrgpu_device_error", "xrgpu_version",
+    "xrgpu_p2p_create", "xrgpu_p2p_connect", "xrgpu_p2p_allgather", "xrgpu_p2p_destroy",
 )
+P2P_HANDLE_BYTES = 64
+P2P_MAX_WORLD = 16
 
 
 class Tensor_(ctypes.Structure):
@@ -90,6 +93,11 @@ def load(path: os.PathLike | None = None):
         "xrgpu_mmnb_dequantize": ([P(Problem_), vp, vp], ctypes.c_int),
         "xrgpu_mmnb_select_path": ([P(Problem_), ctypes.c_char_p, u64], ctypes.c_int),
         "xrgpu_device_error": ([i32, P(ctypes.c_uint32), i32], ctypes.c_int),
+        "xrgpu_p2p_create": ([i32, i32, i32, u64, P(vp), vp], ctypes.c_int),
+        "xrgpu_p2p_connect": ([vp, vp], ctypes.c_int),
+        "xrgpu_p2p_allgather": ([vp, vp, ctypes.c_int64, ctypes.c_int64, vp, ctypes.c_int64, ctypes.c_int64, vp],
+                                ctypes.c_int),
+        "xrgpu_p2p_destroy": ([vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

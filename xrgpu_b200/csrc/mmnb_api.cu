@@ -327,6 +327,8 @@ std::string device_description(int dev) {
 
 }  // namespace
 
+int api_fail(int status, const std::string& message) { return fail(status, message); }
+
 int device_sm_count() {
   static int counts[64] = {0};
   int dev = 0;

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <string>
 
 namespace xrgpu {
 
@@ -54,6 +55,9 @@ cudaError_t launch_gemm(const Problem& p, void* workspace, cudaStream_t s);
 // driver entry point resolved at run time. dtype: 0 = uint8, 1 = float16. Returns false on failure.
 bool encode_tensor_map_2d(void* map, int dtype, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                           uint32_t box_inner, uint32_t box_outer, bool swizzle_128b);
+
+// Records `message` as the calling thread's last error (xrgpu_last_error) and returns `status`.
+int api_fail(int status, const std::string& message);
 
 // Device error word of the current device (nonzero after a kernel's bounded wait expired).
 unsigned* device_error_word();

@@ -1,0 +1,275 @@
+// All-gather of Y shards over NVLink peer memory for column-sharded MatMulNBits (one process per
+// GPU on one node). The reference backend is single-device; this is the exchange step of the
+// N-sharded form, written to replace one NCCL all-gather per projection with a single small kernel
+// that CUDA graphs can capture.
+//
+// Each rank owns one region (cudaMalloc, shared with the other ranks by CUDA IPC):
+//   [0, 256)        done flags: done[q] = last epoch in which rank q finished writing here
+//   [256, ...)      staging[2][world][slot_bytes]: rank q's shard of epoch e lands in staging[e & 1][q]
+// A call on rank r (epoch e, one CTA per peer p):
+//   * p == r: the CTA copies r's own shard into its block of Y;
+//   * p != r: the CTA stores r's shard into p's staging[e & 1][r] (peer stores over NVLink), fences,
+//     sets p's done[r] = e (release, system scope), waits until its own done[p] >= e (acquire,
+//     bounded), then copies p's shard from its own staging into p's block of Y.
+// Staging is double-buffered by epoch parity, so no "ready" handshake is needed: rank r writes
+// staging[e & 1][r] of p again only in epoch e + 2, after it has seen done[p] >= e + 1, which p
+// sets in its call e + 1 -- stream-ordered after p's call e has finished reading staging[e & 1].
+// Every rank must make the same sequence of calls on its group. Waits give up after 1 s and record
+// kErrPeerWait in the device error word (the results of that call are then undefined).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "mmnb_common.cuh"
+#include "mmnb_internal.h"
+#include "xrgpu_mmnb.h"
+
+struct xrgpu_p2p {
+  int device = 0, world = 0, rank = 0;
+  uint64_t slot_bytes = 0, region_bytes = 0;
+  char* local = nullptr;
+  char* peers[XRGPU_P2P_MAX_WORLD] = {};
+  bool opened[XRGPU_P2P_MAX_WORLD] = {};
+  uint32_t* epoch = nullptr;  // device [XRGPU_P2P_MAX_WORLD]: epoch of the last call, per peer
+};
+
+namespace xrgpu {
+namespace {
+
+constexpr int kFlagBytes = 256;
+constexpr int kThreads = 256;  // small enough to sit beside a running GEMV CTA
+constexpr unsigned kErrPeerWait = 0x401;
+
+struct P2PParams {
+  char* peers[XRGPU_P2P_MAX_WORLD];
+  uint32_t* epoch;
+  const char* shard;  // [rows][srb]
+  char* out;          // [rows][orb], rank q's block at byte q * srb, first ovb bytes of a row valid
+  int64_t rows, srb, orb, ovb, slot_bytes;
+  int world, rank;
+  unsigned* err;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Copies `rows` rows of `srb` bytes (16-byte aligned, srb % 16 == 0) from src to dst (row stride
+// orb), keeping only the first `valid` bytes of each row. `cg`: read through L2 only.
+template <bool kCg>
+__device__ void copy_rows(char* dst, int64_t orb, const char* src, int64_t srb, int64_t rows, int64_t valid) {
+  if (valid <= 0) return;
+  const int64_t width = valid < srb ? valid : srb;
+  const int64_t vec = width / 16, total = rows * vec;
+  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
+    const int64_t m = i / vec, j = i - m * vec;
+    const uint4* s = reinterpret_cast<const uint4*>(src + m * srb) + j;
+    const uint4 v = kCg ? __ldcg(s) : *s;
+    *(reinterpret_cast<uint4*>(dst + m * orb) + j) = v;
+  }
+  const int64_t tail = width - vec * 16;  // ragged end of the last block (bytes)
+  for (int64_t i = threadIdx.x; i < rows * tail; i += blockDim.x) {
+    const int64_t m = i / tail, j = vec * 16 + (i - m * tail);
+    const char* s = src + m * srb + j;
+    dst[m * orb + j] = kCg ? static_cast<char>(__ldcg(reinterpret_cast<const unsigned char*>(s))) : *s;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_constant__ P2PParams q) {
+  // Programmatic dependent launch: the next kernel may start (its own griddepcontrol.wait then
+  // waits for this one); this kernel reads the shard only after the previous kernel completed.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int p = static_cast<int>(blockIdx.x);
+  const int64_t block_off = static_cast<int64_t>(p) * q.srb;
+  const int64_t valid = q.ovb - block_off;
+  if (p == q.rank) {
+    copy_rows<false>(q.out + block_off, q.orb, q.shard, q.srb, q.rows, valid);
+    return;
+  }
+  __shared__ uint32_t epoch_s;
+  __shared__ int ok_s;
+  if (threadIdx.x == 0) epoch_s = q.epoch[p] + 1u;
+  __syncthreads();
+  const uint32_t e = epoch_s;
+  const int64_t slot_off = kFlagBytes + (static_cast<int64_t>(e & 1u) * q.world + q.rank) * q.slot_bytes;
+  // 1. this rank's shard into p's staging (contiguous rows * srb bytes, 16-byte vectors)
+  {
+    const int64_t n = q.rows * q.srb / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(q.shard);
+    uint4* dst = reinterpret_cast<uint4*>(q.peers[p] + slot_off);
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  // 2. publish, then wait for p's shard in this rank's staging
+  if (threadIdx.x == 0) {
+    st_release_sys(reinterpret_cast<uint32_t*>(q.peers[p]) + q.rank, e);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(q.peers[q.rank]) + p;
+    int ok = 1;
+    if (static_cast<int32_t>(ld_acquire_sys(mine) - e) < 0) {
+      const uint64_t start = global_timer_ns();
+      while (static_cast<int32_t>(ld_acquire_sys(mine) - e) < 0) {
+        if (global_timer_ns() - start > kWaitLimitNs) {
+          record_device_error(q.err, kErrPeerWait);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    ok_s = ok;
+    q.epoch[p] = e;
+  }
+  __syncthreads();
+  // 3. p's shard from this rank's staging into p's block of Y
+  if (ok_s) {
+    const char* src = q.peers[q.rank] + kFlagBytes + (static_cast<int64_t>(e & 1u) * q.world + p) * q.slot_bytes;
+    copy_rows<true>(q.out + block_off, q.orb, src, q.srb, q.rows, valid);
+  }
+}
+
+}  // namespace
+}  // namespace xrgpu
+
+extern "C" {
+
+int xrgpu_p2p_create(int32_t device, int32_t world, int32_t rank, uint64_t slot_bytes, xrgpu_p2p** group,
+                     void* ipc_handle) {
+  using namespace xrgpu;
+  if (!group || !ipc_handle) return api_fail(XRGPU_INVALID_ARGUMENT, "null group or handle pointer");
+  *group = nullptr;
+  if (world < 1 || world > XRGPU_P2P_MAX_WORLD || rank < 0 || rank >= world)
+    return api_fail(XRGPU_INVALID_ARGUMENT, "world must be in [1, 16] and rank in [0, world)");
+  if (slot_bytes == 0 || slot_bytes % 16) return api_fail(XRGPU_INVALID_ARGUMENT, "slot_bytes must be a positive multiple of 16");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (cudaSetDevice(device) != cudaSuccess) return api_fail(XRGPU_UNAVAILABLE, "cannot select the CUDA device");
+  xrgpu_p2p* g = new (std::nothrow) xrgpu_p2p();
+  int st = XRGPU_OK;
+  if (!g) {
+    st = api_fail(XRGPU_RUNTIME_ERROR, "out of host memory");
+  } else {
+    g->device = device;
+    g->world = world;
+    g->rank = rank;
+    g->slot_bytes = align_up(slot_bytes, 256);
+    g->region_bytes = kFlagBytes + 2 * static_cast<uint64_t>(world) * g->slot_bytes;
+    cudaIpcMemHandle_t h;
+    if (cudaMalloc(&g->local, g->region_bytes) != cudaSuccess || cudaMemset(g->local, 0, g->region_bytes) != cudaSuccess ||
+        cudaMalloc(&g->epoch, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD) != cudaSuccess ||
+        cudaMemset(g->epoch, 0, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&h, g->local) != cudaSuccess) {
+      st = api_fail(XRGPU_RUNTIME_ERROR, "peer-memory region allocation or IPC export failed");
+    } else {
+      std::memcpy(ipc_handle, &h, sizeof(h));
+      g->peers[rank] = g->local;
+      *group = g;
+    }
+  }
+  if (st != XRGPU_OK && g) {
+    if (g->local) cudaFree(g->local);
+    if (g->epoch) cudaFree(g->epoch);
+    delete g;
+  }
+  cudaSetDevice(prev);
+  return st;
+}
+
+int xrgpu_p2p_connect(xrgpu_p2p* g, const void* ipc_handles) {
+  using namespace xrgpu;
+  if (!g || !ipc_handles) return api_fail(XRGPU_INVALID_ARGUMENT, "null group or handles");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(g->device);
+  int st = XRGPU_OK;
+  for (int p = 0; p < g->world && st == XRGPU_OK; ++p) {
+    if (p == g->rank || g->opened[p]) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(ipc_handles) + static_cast<size_t>(p) * XRGPU_P2P_HANDLE_BYTES, sizeof(h));
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      st = api_fail(XRGPU_RUNTIME_ERROR, "cannot open rank " + std::to_string(p) + "'s peer-memory region");
+    } else {
+      g->peers[p] = static_cast<char*>(ptr);
+      g->opened[p] = true;
+    }
+  }
+  cudaSetDevice(prev);
+  return st;
+}
+
+int xrgpu_p2p_allgather(xrgpu_p2p* g, const void* shard, int64_t rows, int64_t shard_row_bytes, void* out,
+                        int64_t out_row_bytes, int64_t out_valid_bytes, void* stream) {
+  using namespace xrgpu;
+  if (!g || !shard || !out) return api_fail(XRGPU_INVALID_ARGUMENT, "null group, shard or output");
+  for (int p = 0; p < g->world; ++p)
+    if (!g->peers[p]) return api_fail(XRGPU_INVALID_ARGUMENT, "group not connected (xrgpu_p2p_connect)");
+  if (rows < 0 || shard_row_bytes <= 0 || shard_row_bytes % 16 || (rows > 1 && out_row_bytes % 16) ||
+      out_valid_bytes > out_row_bytes || out_valid_bytes > shard_row_bytes * g->world ||
+      out_valid_bytes <= shard_row_bytes * (g->world - 1))
+    return api_fail(XRGPU_INVALID_ARGUMENT,
+                    "need shard_row_bytes % 16 == 0, out_row_bytes % 16 == 0 (more than one row) and "
+                    "(world-1)*shard < valid <= min(out_row_bytes, world*shard)");
+  if (static_cast<uint64_t>(rows * shard_row_bytes) > g->slot_bytes)
+    return api_fail(XRGPU_INVALID_ARGUMENT, "shard larger than the group's slot_bytes");
+  if ((reinterpret_cast<uintptr_t>(shard) | reinterpret_cast<uintptr_t>(out)) % 16)
+    return api_fail(XRGPU_INVALID_ARGUMENT, "shard and output must be 16-byte aligned");
+  if (rows == 0) return XRGPU_OK;
+  P2PParams q{};
+  for (int p = 0; p < g->world; ++p) q.peers[p] = g->peers[p];
+  q.epoch = g->epoch;
+  q.shard = static_cast<const char*>(shard);
+  q.out = static_cast<char*>(out);
+  q.rows = rows;
+  q.srb = shard_row_bytes;
+  q.orb = out_row_bytes;
+  q.ovb = out_valid_bytes;
+  q.slot_bytes = static_cast<int64_t>(g->slot_bytes);
+  q.world = g->world;
+  q.rank = g->rank;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(g->device);
+  q.err = device_error_word();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(g->world), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, p2p_allgather_kernel, q);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return api_fail(XRGPU_RUNTIME_ERROR, std::string("peer all-gather launch failed: ") + cudaGetErrorString(e));
+  return XRGPU_OK;
+}
+
+int xrgpu_p2p_destroy(xrgpu_p2p* g) {
+  using namespace xrgpu;
+  if (!g) return XRGPU_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(g->device);
+  int st = XRGPU_OK;
+  for (int p = 0; p < g->world; ++p)
+    if (g->opened[p] && cudaIpcCloseMemHandle(g->peers[p]) != cudaSuccess)
+      st = api_fail(XRGPU_RUNTIME_ERROR, "closing a peer-memory mapping failed");
+  if (g->local) cudaFree(g->local);
+  if (g->epoch) cudaFree(g->epoch);
+  cudaSetDevice(prev);
+  delete g;
+  return st;
+}
+
+}  // extern "C"

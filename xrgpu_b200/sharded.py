@@ -7,12 +7,16 @@ tensors, computes its columns of Y with this package's kernels (A is replicated)
 all-gather (NCCL over NVLink/NVSwitch) assembles Y. The reference backend is single-device;
 the contract (inputs, attributes, output shape and values) is unchanged.
 
-Shards are equal (``ceil(N / world)`` columns, the last one padded) so that the gather is one
-``all_gather_into_tensor``; for M == 1 the gathered buffer already is Y, for M > 1 one permute
-copy turns ``[world, M, S]`` into ``[M, world * S]``.
+Shards are equal (``ceil(N / world)`` columns, the last one padded). On NCCL groups of one node,
+shards up to ``peer_max_bytes`` are exchanged by this package's peer-memory all-gather (one kernel
+over NVLink that writes Y directly, no NCCL call, so a step can be captured in a CUDA graph);
+larger shards and gloo groups use ``all_gather_into_tensor`` / ``all_gather`` (for M == 1 the
+gathered buffer already is Y, for M > 1 one permute copy turns ``[world, M, S]`` into
+``[M, world * S]``).
 """
 from __future__ import annotations
 
+import os
 from typing import Callable, Optional
 
 import torch
@@ -54,7 +58,8 @@ class ShardedMatMulNBits:
 
     def __init__(self, b: torch.Tensor, scales: torch.Tensor, zero_points: Optional[torch.Tensor] = None,
                  bias: Optional[torch.Tensor] = None, *, K: int, N: int, bits: int = 4, block_size: int,
-                 group=None, compute: Optional[Callable] = None, _presharded: bool = False):
+                 group=None, compute: Optional[Callable] = None, peer_gather: Optional[bool] = None,
+                 peer_max_bytes: int = 4 << 20, peer_group=None, _presharded: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -71,13 +76,49 @@ class ShardedMatMulNBits:
         if self.b.shape[0] != self.n1 - self.n0:
             raise ValueError(f"rank {self.rank} shard has {self.b.shape[0]} columns, expected {self.n1 - self.n0}")
         self.compute = compute or F.matmul_nbits
-
+        # Peer-memory all-gather: NCCL groups whose ranks all live on this node (torchrun's
+        # LOCAL_WORLD_SIZE), unless disabled; created lazily by the first eligible forward, which
+        # every rank makes with the same shapes.
+        same_node = int(os.environ.get("LOCAL_WORLD_SIZE", self.world)) == self.world
+        auto = (self.world > 1 and dist.is_initialized() and dist.get_backend(group) == "nccl" and same_node)
+        self.peer_gather = auto if peer_gather is None else (bool(peer_gather) and self.world > 1)
+        self.peer_max_bytes = int(peer_max_bytes)
+        # A PeerAllGather shared with other modules (owned by the caller), or this module's own.
+        self._shared_peer = peer_group
+        self._peer = None
     @classmethod
     def from_shard(cls, b_shard: torch.Tensor, scales_shard: torch.Tensor, zero_points_shard=None, bias_shard=None,
-                   *, K: int, N: int, bits: int = 4, block_size: int, group=None, compute=None):
+                   *, K: int, N: int, bits: int = 4, block_size: int, group=None, compute=None, **kw):
         """Build from this rank's slices (rows shard_bounds(N, world, rank) of each tensor)."""
         return cls(b_shard, scales_shard, zero_points_shard, bias_shard, K=K, N=N, bits=bits,
-                   block_size=block_size, group=group, compute=compute, _presharded=True)
+                   block_size=block_size, group=group, compute=compute, _presharded=True, **kw)
+
+    def uses_peer_gather(self, M: int, element_size: int = 2) -> bool:
+        """Whether forward with M rows exchanges Y through peer memory (no NCCL call)."""
+        return (self.peer_gather and M * self.S * element_size <= self.peer_max_bytes
+                and (self.S * element_size) % 16 == 0 and (M == 1 or (self.N * element_size) % 16 == 0))
+
+    def set_peer_group(self, peer_group) -> None:
+        """Use a PeerAllGather shared with other modules (the caller closes it)."""
+        self._shared_peer = peer_group
+
+    def _peer_group(self, nbytes: int):
+        from .p2p import PeerAllGather
+        if self._shared_peer is not None:
+            if self._shared_peer.slot_bytes < nbytes:
+                raise ValueError(f"shared peer group slot ({self._shared_peer.slot_bytes} B) < shard ({nbytes} B)")
+            return self._shared_peer
+        if self._peer is None or self._peer.slot_bytes < nbytes:
+            if self._peer is not None:
+                self._peer.close()
+            self._peer = PeerAllGather(max(nbytes, 1 << 16), group=self.group)
+        return self._peer
+
+    def close(self):
+        """Release this module's own peer-memory group (collective: every rank calls it)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def local(self, a: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """This rank's columns of Y into out[..., :n1 - n0] (out is [M, S], S >= n1 - n0)."""
@@ -103,6 +144,10 @@ class ShardedMatMulNBits:
                 out.view(M, self.N).copy_(y)
                 return out
             return y.reshape(*lead, self.N)
+        if self.uses_peer_gather(M, y_local.element_size()):
+            dst = out.view(M, self.N) if out is not None else torch.empty((M, self.N), dtype=a.dtype, device=a.device)
+            self._peer_group(M * self.S * y_local.element_size()).all_gather(y_local, dst, self.N)
+            return out if out is not None else dst.reshape(*lead, self.N)
         direct = out is not None and M == 1 and self.world * self.S == self.N and out.is_contiguous()
         gathered = (out.view(self.world, 1, self.S) if direct
                     else torch.empty((self.world, M, self.S), dtype=a.dtype, device=a.device))
