@@ -11,6 +11,10 @@ Workloads (synthetic seeded data of their shapes/distribu
       uint8 zero points (nibbles uniform in [0,15]). metric GB/s of algorithmic bytes
       (B + scales + zero points + A + Y).
   batched_decode_m{4,16,64} (config 3), prefill_m2048 (config 4, TFLOP/s), oracle_case (config 1).
+  llama70b_shard_decode / llama70b_shard_prefill (config 5): one GPU's 1/8 column shard of the
+      70B-scale projections (K, N) = (8192, 28672), (28672, 8192), (8192, 128256), i.e. (8192,3584),
+      (28672,1024), (8192,16032), at M=1 (GB/s) and M=4096 (TFLOP/s); bs 32, packed zero points.
+      With --gpus 8 the weak-scaled step is exactly the full config-5 problem.
 Each step uses a different copy ("layer") of the weights; the copies total > 3x the 126 MB L2,
 so every step streams its weights from HBM (config: "l2": "rotating weight copies > L2").
 
@@ -54,6 +58,10 @@ WORKLOADS = {
     "batched_decode_m16": dict(config=3, M=16, bs=128, zp=True, scale=(0.002, 0.01), proj=[("ffn", 4096, 14336)], kind="decode"),
     "batched_decode_m64": dict(config=3, M=64, bs=128, zp=True, scale=(0.002, 0.01), proj=[("ffn", 4096, 14336)], kind="decode"),
     "prefill_m2048": dict(config=4, M=2048, bs=64, zp=False, scale=(0.005, 0.02), proj=[("ffn", 4096, 14336)], kind="prefill"),
+    "llama70b_shard_decode": dict(config=5, M=1, bs=32, zp=True, scale=(0.005, 0.02), kind="decode",
+                                  proj=[("up", 8192, 3584), ("down", 28672, 1024), ("lm_head", 8192, 16032)]),
+    "llama70b_shard_prefill": dict(config=5, M=4096, bs=32, zp=True, scale=(0.005, 0.02), kind="prefill",
+                                   proj=[("up", 8192, 3584), ("down", 28672, 1024), ("lm_head", 8192, 16032)]),
     "oracle_case": dict(config=1, M=1, bs=32, zp=False, scale=(0.005, 0.02), proj=[("proj", 4096, 4096)], kind="decode",
                         dtype="float32"),
 }

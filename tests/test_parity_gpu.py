@@ -245,6 +245,29 @@ def test_gemm_prefill_full_size_properties(F):
         assert ok, st
 
 
+@pytest.mark.parametrize("M", [1, 4096])
+def test_config5_shard_full_size(F, M):
+    """Config 5 (70B-scale, bs 32, packed zero points): one GPU's 1/8 shard of the lm_head
+    projection, (K, N) = (8192, 16032), at decode (GEMV) and prefill (GEMM) size: deterministic
+    and within the tolerance of the oracle on a row x column sample."""
+    rng = np.random.default_rng(5)
+    K, N, bs = 8192, 16032, 32
+    a, b, s, zp, _ = make(rng, M, K, N, 4, bs, np.float16, "packed")
+    da, db, ds, dz = dev(a), dev(b), dev(s), dev(zp)
+    assert F.select_path(da, db, ds, dz, K=K, N=N, block_size=bs) == ("gemv" if M == 1 else "gemm")
+    y1 = F.matmul_nbits(da, db, ds, dz, K=K, N=N, block_size=bs)
+    y2 = F.matmul_nbits(da, db, ds, dz, K=K, N=N, block_size=bs)
+    torch.cuda.synchronize()
+    assert F.device_error(0) == 0
+    assert torch.equal(y1, y2)
+    rows = np.r_[0:min(M, 32), max(0, M - 32):M] if M > 1 else np.r_[0:1]
+    y_host = y1.cpu().numpy()
+    for cs in (slice(0, 256), slice(N - 256, N)):
+        ref = O.matmul_nbits(a[rows], b, s, zp, K=K, N=N, bits=4, block_size=bs, columns=cs)
+        ok, st = within_baseline_tol(y_host[rows][:, cs], ref)
+        assert ok, (M, cs, st)
+
+
 def test_gemm_writes_strided_output_slice(F):
     rng = np.random.default_rng(6)
     M, K, N, bs = 80, 1024, 160, 32
