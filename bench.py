@@ -249,7 +249,27 @@ def run_ours(args, wl):
                 for p in layer:
                     p["mod"].set_peer_group(shared)
 
+    # With N > 1 ranks and peer-memory all-gathers, a projection's all-gather may overlap the GEMVs
+    # that do not depend on its Y: in a decoder layer q, k, v share their input, o needs attention
+    # over all three, gate and up share their input and down needs both. Each group's gathers are
+    # joined before the next group starts, so the gathers of v, o, up and down stay exposed.
+    order = [p["name"] for p in weights[0]]
+    layer_groups = [["q", "k", "v"], ["o"], ["gate", "up"], ["down"]]
+    if sorted(order) != sorted(n for grp in layer_groups for n in grp):
+        layer_groups = [[n] for n in order]  # other workloads: each projection depends on the last
+    overlap = world > 1 and shared is not None and not args.no_overlap
+    comm = torch.cuda.Stream(device) if overlap else None
+
     def step(layer, gather=True):
+        by_name = {p["name"]: p for p in weights[layer]}
+        if world > 1 and gather and overlap:
+            for grp in layer_groups:
+                for name in grp:
+                    p = by_name[name]
+                    p["mod"](acts[p["K"]], out=gathered[(p["name"], p["N"])], gather_stream=comm)
+                for name in grp:
+                    by_name[name]["mod"].wait_gather()
+            return
         for p in weights[layer]:
             if world > 1 and gather:
                 p["mod"](acts[p["K"]], out=gathered[(p["name"], p["N"])])
@@ -436,7 +456,8 @@ def run_ours(args, wl):
                    "projections": [[n, K, N] for (n, K, N) in wl["proj"]], "bits": 4, "block_size": wl["bs"],
                    "zero_points": "packed uint8" if wl["zp"] else "none", "l2": f"{layers} rotating weight copies "
                    f"({layers * per_layer / 1e6:.0f} MB > 3x L2)", "parallelism": f"column-shard x{world}" +
-                   ((" + peer-memory all-gather of Y" if peer else " + NCCL all-gather of Y") if world > 1 else ""),
+                   ((" + peer-memory all-gather of Y" + (" overlapped within q/k/v and gate/up" if overlap and any(len(g) > 1 for g in layer_groups) else "")
+                    if peer else " + NCCL all-gather of Y") if world > 1 else ""),
                    "cuda_graphs": use_graphs, "paths": paths},
         "roofline": roofline, "kernels_us": kernel, "gpu_launches": launches_per_step * args.steps,
         "clocks": clock, "e2e": e2e, "cpu_baseline": cpu,
@@ -522,6 +543,8 @@ def main():
     ap.add_argument("--seed", type=int, default=2024)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="N > 1: run every all-gather on the compute stream (no overlap with independent GEMVs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()

@@ -171,6 +171,13 @@ def _peer_rank(rank, world, port, results):
                 torch.cuda.synchronize()
                 ok &= torch.equal(y_out, nccl(x_in))
             del g
+            # overlapped form: the gather runs on a side stream; Y is complete after wait_gather()
+            side = torch.cuda.Stream()
+            for rep in range(2):
+                x = d(a) * (0.75 + rep)
+                y_side = peer(x, gather_stream=side)
+                peer.wait_gather()
+                ok &= torch.equal(y_side, nccl(x))
             # the single-GPU kernel agrees to the tolerance (its K split may differ)
             y_one = F.matmul_nbits(d(a), d(b), d(s), d(zp), d(bb), K=K, N=N, block_size=bs)
             ok &= bool((peer(d(a)).float() - y_one.float()).abs().max().item() <= 2e-3 * y_one.float().abs().max().item())

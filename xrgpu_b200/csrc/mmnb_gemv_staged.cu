@@ -26,6 +26,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "mmnb_common.cuh"
 
@@ -450,10 +451,17 @@ size_t staged_smem(const Problem& p) {
 
 template <int BS, int ZM>
 cudaError_t launch_staged_variant(const StagedParams& gp, int grid, size_t smem, cudaStream_t stream) {
-  if (smem > 48 * 1024) {
+  // The dynamic shared-memory limit is raised to the maximum once per device (a host call per
+  // launch would add microseconds to every decode step launched eagerly).
+  static std::atomic<uint64_t> raised{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (smem > 48 * 1024 && !(raised.load(std::memory_order_acquire) & bit)) {
     const cudaError_t e = cudaFuncSetAttribute(gemv_staged_kernel<BS, ZM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(smem));
+                                               kMaxSmem);
     if (e != cudaSuccess) return e;
+    raised.fetch_or(bit, std::memory_order_acq_rel);
   }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);

@@ -92,8 +92,11 @@ def matmul_nbits(a: torch.Tensor, b: torch.Tensor, scales: torch.Tensor, zero_po
     ws_ptr, ws_bytes = None, 0
     if workspace is not None:
         ws_ptr, ws_bytes = ctypes.c_void_p(workspace.data_ptr()), workspace.numel() * workspace.element_size()
-    with torch.cuda.device(dev):
+    if torch.cuda.current_device() == dev.index:
         check(lib.xrgpu_mmnb_forward(ctypes.byref(p), ws_ptr, ws_bytes, ctypes.c_void_p(stream)))
+    else:
+        with torch.cuda.device(dev):
+            check(lib.xrgpu_mmnb_forward(ctypes.byref(p), ws_ptr, ws_bytes, ctypes.c_void_p(stream)))
     return out
 
 

@@ -86,6 +86,8 @@ class ShardedMatMulNBits:
         # A PeerAllGather shared with other modules (owned by the caller), or this module's own.
         self._shared_peer = peer_group
         self._peer = None
+        self._y_buf = None        # shard buffer of the overlapped form (see forward)
+        self._gather_done = None  # event of the last overlapped gather
     @classmethod
     def from_shard(cls, b_shard: torch.Tensor, scales_shard: torch.Tensor, zero_points_shard=None, bias_shard=None,
                    *, K: int, N: int, bits: int = 4, block_size: int, group=None, compute=None, **kw):
@@ -130,13 +132,27 @@ class ShardedMatMulNBits:
             out[:, n_local:].zero_()
         return out
 
-    def forward(self, a: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def forward(self, a: torch.Tensor, out: Optional[torch.Tensor] = None,
+                gather_stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
         """Full Y [*, N] on every rank. `out` (contiguous, Y's shape) receives it without an extra
-        copy when M == 1 and N is a multiple of the group size."""
+        copy when M == 1 and N is a multiple of the group size.
+
+        gather_stream (peer-memory all-gather only): the all-gather runs on that stream after the
+        local kernel, so the calling stream can go on with independent work; Y is complete once
+        the caller has made its stream wait with ``wait_gather()``. The shard buffer is then this
+        module's own and is reused by its next call, so call ``wait_gather()`` before calling the
+        module again. Every rank must issue its gathers in the same order on its group."""
         lead = tuple(a.shape[:-1])
         M = a.numel() // self.K
         a2 = a.reshape(M, self.K)
-        y_local = torch.empty((M, self.S), dtype=a.dtype, device=a.device)
+        overlap = gather_stream is not None and self.world > 1 and self.uses_peer_gather(M, a.element_size())
+        if overlap:
+            key = (M, a.dtype, a.device)
+            if self._y_buf is None or self._y_buf[0] != key:
+                self._y_buf = (key, torch.empty((M, self.S), dtype=a.dtype, device=a.device))
+            y_local = self._y_buf[1]
+        else:
+            y_local = torch.empty((M, self.S), dtype=a.dtype, device=a.device)
         self.local(a2, y_local)
         if self.world == 1:
             y = y_local[:, :self.N]
@@ -146,7 +162,17 @@ class ShardedMatMulNBits:
             return y.reshape(*lead, self.N)
         if self.uses_peer_gather(M, y_local.element_size()):
             dst = out.view(M, self.N) if out is not None else torch.empty((M, self.N), dtype=a.dtype, device=a.device)
-            self._peer_group(M * self.S * y_local.element_size()).all_gather(y_local, dst, self.N)
+            group = self._peer_group(M * self.S * y_local.element_size())
+            if overlap:
+                ready = torch.cuda.Event()
+                ready.record()
+                gather_stream.wait_event(ready)
+                with torch.cuda.stream(gather_stream):
+                    group.all_gather(y_local, dst, self.N)
+                    self._gather_done = torch.cuda.Event()
+                    self._gather_done.record()
+            else:
+                group.all_gather(y_local, dst, self.N)
             return out if out is not None else dst.reshape(*lead, self.N)
         direct = out is not None and M == 1 and self.world * self.S == self.N and out.is_contiguous()
         gathered = (out.view(self.world, 1, self.S) if direct
@@ -165,5 +191,12 @@ class ShardedMatMulNBits:
             out.view(M, self.N).copy_(y)
             return out
         return y.reshape(*lead, self.N)
+
+    def wait_gather(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Make `stream` (default: the current one) wait for the last gather issued on a
+        gather_stream; a no-op when none is pending."""
+        if self._gather_done is not None:
+            (stream or torch.cuda.current_stream()).wait_event(self._gather_done)
+            self._gather_done = None
 
     __call__ = forward
