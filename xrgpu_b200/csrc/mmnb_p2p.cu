@@ -4,13 +4,16 @@
 // that CUDA graphs can capture.
 //
 // Each rank owns one region (cudaMalloc, shared with the other ranks by CUDA IPC):
-//   [0, 256)        done flags: done[q] = last epoch in which rank q finished writing here
+//   [0, 256)        done flags: done[q][c] = last epoch in which rank q finished writing chunk c here
 //   [256, ...)      staging[2][world][slot_bytes]: rank q's shard of epoch e lands in staging[e & 1][q]
-// A call on rank r (epoch e, one CTA per peer p):
-//   * p == r: the CTA copies r's own shard into its block of Y;
-//   * p != r: the CTA stores r's shard into p's staging[e & 1][r] (peer stores over NVLink), fences,
-//     sets p's done[r] = e (release, system scope), waits until its own done[p] >= e (acquire,
-//     bounded), then copies p's shard from its own staging into p's block of Y.
+// The shard (rows x row bytes, contiguous) is cut into kChunks byte chunks. A call on rank r (epoch
+// e) runs one CTA per (peer p, chunk c):
+//   * p == r: the CTA copies chunk c of r's own shard into r's block of Y;
+//   * p != r: the CTA stores chunk c of r's shard into p's staging[e & 1][r] (peer stores over
+//     NVLink), and after a CTA barrier one thread sets p's done[r][c] = e with a release store at
+//     system scope (the barrier orders every thread's stores before it, and release is cumulative);
+//     it then waits until its own done[p][c] >= e (acquire, bounded) and copies chunk c of p's shard
+//     from its own staging into p's block of Y.
 // Staging is double-buffered by epoch parity, so no "ready" handshake is needed: rank r writes
 // staging[e & 1][r] of p again only in epoch e + 2, after it has seen done[p] >= e + 1, which p
 // sets in its call e + 1 -- stream-ordered after p's call e has finished reading staging[e & 1].
@@ -33,7 +36,7 @@ struct xrgpu_p2p {
   char* local = nullptr;
   char* peers[XRGPU_P2P_MAX_WORLD] = {};
   bool opened[XRGPU_P2P_MAX_WORLD] = {};
-  uint32_t* epoch = nullptr;  // device [XRGPU_P2P_MAX_WORLD]: epoch of the last call, per peer
+  uint32_t* epoch = nullptr;  // device [XRGPU_P2P_MAX_WORLD * 4]: epoch of the last call, per (peer, chunk)
 };
 
 namespace xrgpu {
@@ -41,6 +44,8 @@ namespace {
 
 constexpr int kFlagBytes = 256;
 constexpr int kThreads = 256;  // small enough to sit beside a running GEMV CTA
+constexpr int kChunks = 4;     // CTAs per peer: the peer stores of one shard spread over 4 SMs
+static_assert(XRGPU_P2P_MAX_WORLD * kChunks * 4 <= kFlagBytes, "done flags must fit the flag area");
 constexpr unsigned kErrPeerWait = 0x401;
 
 struct P2PParams {
@@ -62,24 +67,25 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// Copies `rows` rows of `srb` bytes (16-byte aligned, srb % 16 == 0) from src to dst (row stride
-// orb), keeping only the first `valid` bytes of each row. `cg`: read through L2 only.
+// Copies bytes [lo, hi) of a contiguous [rows][srb] shard (lo, hi and srb multiples of 16) into
+// the rows of dst (row stride orb), keeping only the first `valid` bytes of each row. kCg: read
+// the source through L2 only (it was written by another GPU).
 template <bool kCg>
-__device__ void copy_rows(char* dst, int64_t orb, const char* src, int64_t srb, int64_t rows, int64_t valid) {
+__device__ void copy_chunk(char* dst, int64_t orb, const char* src, int64_t srb, int64_t lo, int64_t hi, int64_t valid) {
   if (valid <= 0) return;
   const int64_t width = valid < srb ? valid : srb;
-  const int64_t vec = width / 16, total = rows * vec;
-  for (int64_t i = threadIdx.x; i < total; i += blockDim.x) {
-    const int64_t m = i / vec, j = i - m * vec;
-    const uint4* s = reinterpret_cast<const uint4*>(src + m * srb) + j;
-    const uint4 v = kCg ? __ldcg(s) : *s;
-    *(reinterpret_cast<uint4*>(dst + m * orb) + j) = v;
-  }
-  const int64_t tail = width - vec * 16;  // ragged end of the last block (bytes)
-  for (int64_t i = threadIdx.x; i < rows * tail; i += blockDim.x) {
-    const int64_t m = i / tail, j = vec * 16 + (i - m * tail);
-    const char* s = src + m * srb + j;
-    dst[m * orb + j] = kCg ? static_cast<char>(__ldcg(reinterpret_cast<const unsigned char*>(s))) : *s;
+  for (int64_t o = lo + 16 * static_cast<int64_t>(threadIdx.x); o < hi; o += 16 * static_cast<int64_t>(blockDim.x)) {
+    const int64_t m = o / srb, j = o - m * srb;
+    if (j >= width) continue;
+    const uint4* s = reinterpret_cast<const uint4*>(src + o);
+    if (j + 16 <= width) {
+      const uint4 v = kCg ? __ldcg(s) : *s;
+      *reinterpret_cast<uint4*>(dst + m * orb + j) = v;
+    } else {  // ragged end of the last block
+      for (int64_t t = j; t < width; ++t)
+        dst[m * orb + t] = kCg ? static_cast<char>(__ldcg(reinterpret_cast<const unsigned char*>(src + m * srb + t)))
+                               : src[m * srb + t];
+    }
   }
 }
 
@@ -88,32 +94,34 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
   // waits for this one); this kernel reads the shard only after the previous kernel completed.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int p = static_cast<int>(blockIdx.x);
+  const int p = static_cast<int>(blockIdx.x) / kChunks, c = static_cast<int>(blockIdx.x) % kChunks;
+  const int64_t bytes = q.rows * q.srb;
+  const int64_t per = (bytes / 16 + kChunks - 1) / kChunks * 16;
+  const int64_t lo = per * c < bytes ? per * c : bytes, hi = per * (c + 1) < bytes ? per * (c + 1) : bytes;
   const int64_t block_off = static_cast<int64_t>(p) * q.srb;
   const int64_t valid = q.ovb - block_off;
   if (p == q.rank) {
-    copy_rows<false>(q.out + block_off, q.orb, q.shard, q.srb, q.rows, valid);
+    copy_chunk<false>(q.out + block_off, q.orb, q.shard, q.srb, lo, hi, valid);
     return;
   }
   __shared__ uint32_t epoch_s;
   __shared__ int ok_s;
-  if (threadIdx.x == 0) epoch_s = q.epoch[p] + 1u;
+  uint32_t* epoch = q.epoch + p * kChunks + c;
+  if (threadIdx.x == 0) epoch_s = *epoch + 1u;
   __syncthreads();
   const uint32_t e = epoch_s;
   const int64_t slot_off = kFlagBytes + (static_cast<int64_t>(e & 1u) * q.world + q.rank) * q.slot_bytes;
-  // 1. this rank's shard into p's staging (contiguous rows * srb bytes, 16-byte vectors)
+  // 1. chunk c of this rank's shard into p's staging (16-byte vectors)
   {
-    const int64_t n = q.rows * q.srb / 16;
-    const uint4* src = reinterpret_cast<const uint4*>(q.shard);
-    uint4* dst = reinterpret_cast<uint4*>(q.peers[p] + slot_off);
-    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    const uint4* src = reinterpret_cast<const uint4*>(q.shard + lo);
+    uint4* dst = reinterpret_cast<uint4*>(q.peers[p] + slot_off + lo);
+    for (int64_t i = threadIdx.x; i < (hi - lo) / 16; i += blockDim.x) dst[i] = src[i];
   }
-  __threadfence_system();
   __syncthreads();
-  // 2. publish, then wait for p's shard in this rank's staging
+  // 2. publish (release, system scope), then wait for p's chunk in this rank's staging
   if (threadIdx.x == 0) {
-    st_release_sys(reinterpret_cast<uint32_t*>(q.peers[p]) + q.rank, e);
-    const uint32_t* mine = reinterpret_cast<const uint32_t*>(q.peers[q.rank]) + p;
+    st_release_sys(reinterpret_cast<uint32_t*>(q.peers[p]) + q.rank * kChunks + c, e);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(q.peers[q.rank]) + p * kChunks + c;
     int ok = 1;
     if (static_cast<int32_t>(ld_acquire_sys(mine) - e) < 0) {
       const uint64_t start = global_timer_ns();
@@ -123,17 +131,17 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
           ok = 0;
           break;
         }
-        __nanosleep(64);
+        __nanosleep(32);
       }
     }
     ok_s = ok;
-    q.epoch[p] = e;
+    *epoch = e;
   }
   __syncthreads();
-  // 3. p's shard from this rank's staging into p's block of Y
+  // 3. chunk c of p's shard from this rank's staging into p's block of Y
   if (ok_s) {
     const char* src = q.peers[q.rank] + kFlagBytes + (static_cast<int64_t>(e & 1u) * q.world + p) * q.slot_bytes;
-    copy_rows<true>(q.out + block_off, q.orb, src, q.srb, q.rows, valid);
+    copy_chunk<true>(q.out + block_off, q.orb, src, q.srb, lo, hi, valid);
   }
 }
 
@@ -165,8 +173,8 @@ int xrgpu_p2p_create(int32_t device, int32_t world, int32_t rank, uint64_t slot_
     g->region_bytes = kFlagBytes + 2 * static_cast<uint64_t>(world) * g->slot_bytes;
     cudaIpcMemHandle_t h;
     if (cudaMalloc(&g->local, g->region_bytes) != cudaSuccess || cudaMemset(g->local, 0, g->region_bytes) != cudaSuccess ||
-        cudaMalloc(&g->epoch, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD) != cudaSuccess ||
-        cudaMemset(g->epoch, 0, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD) != cudaSuccess ||
+        cudaMalloc(&g->epoch, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD * kChunks) != cudaSuccess ||
+        cudaMemset(g->epoch, 0, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD * kChunks) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&h, g->local) != cudaSuccess) {
       st = api_fail(XRGPU_RUNTIME_ERROR, "peer-memory region allocation or IPC export failed");
     } else {
@@ -241,7 +249,7 @@ int xrgpu_p2p_allgather(xrgpu_p2p* g, const void* shard, int64_t rows, int64_t s
   cudaSetDevice(g->device);
   q.err = device_error_word();
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(g->world), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(g->world * kChunks), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
