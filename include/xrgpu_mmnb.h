@@ -215,7 +215,7 @@ XRGPU_API int xrgpu_device_error(int32_t device, uint32_t* code, int32_t clear);
 #define XRGPU_P2P_HANDLE_BYTES 64
 typedef struct xrgpu_p2p xrgpu_p2p;
 
-/* Allocates this rank's staging region on `device` (2 * world * slot_bytes + 256 bytes, zero-filled)
+/* Allocates this rank's staging region on `device` (2 * world * slot_bytes + 4 KB, zero-filled)
  * and writes its 64-byte CUDA IPC handle to ipc_handle. slot_bytes: largest shard in bytes (a
  * multiple of 16). */
 XRGPU_API int xrgpu_p2p_create(int32_t device, int32_t world, int32_t rank, uint64_t slot_bytes, xrgpu_p2p** group,

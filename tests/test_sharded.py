@@ -142,8 +142,10 @@ def _peer_rank(rank, world, port, results):
     mods = []
     try:
         from xrgpu_b200 import functional as F
-        # (M, K, N, bs): shards of 2048 / 2056 columns (16-byte rows); N = 4111 pads the last shard
-        for i, (M, K, N, bs) in enumerate([(1, 4096, 4096, 32), (1, 4096, 4111, 32), (4, 2048, 1024, 64)]):
+        # (M, K, N, bs): shards of 2048 / 2056 columns (16-byte rows); N = 4111 pads the last shard;
+        # M = 512 gives 2 MB shards, cut into 8 chunks per peer
+        for i, (M, K, N, bs) in enumerate([(1, 4096, 4096, 32), (1, 4096, 4111, 32), (4, 2048, 1024, 64),
+                                           (512, 1024, 4096, 64)]):
             a, b, s, zp, bb = _case(200 + i, M, K, N, bs, "packed", True)
             d = lambda x: None if x is None else torch.from_numpy(x).cuda()  # noqa: E731
             peer = ShardedMatMulNBits(d(b), d(s), d(zp), d(bb), K=K, N=N, block_size=bs, peer_gather=True)
@@ -196,4 +198,4 @@ def test_peer_allgather_two_gpus_matches_nccl():
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     mp.start_processes(_peer_rank, args=(2, _free_port(), results), nprocs=2, start_method="spawn")
-    assert all(results.get((r, i), False) for r in range(2) for i in range(3)), dict(results)
+    assert all(results.get((r, i), False) for r in range(2) for i in range(4)), dict(results)

@@ -4,10 +4,11 @@
 // that CUDA graphs can capture.
 //
 // Each rank owns one region (cudaMalloc, shared with the other ranks by CUDA IPC):
-//   [0, 256)        done flags: done[q][c] = last epoch in which rank q finished writing chunk c here
-//   [256, ...)      staging[2][world][slot_bytes]: rank q's shard of epoch e lands in staging[e & 1][q]
-// The shard (rows x row bytes, contiguous) is cut into kChunks byte chunks. A call on rank r (epoch
-// e) runs one CTA per (peer p, chunk c):
+//   [0, 4 KB)       done flags: done[q][c] = last epoch in which rank q finished writing chunk c here
+//   [4 KB, ...)     staging[2][world][slot_bytes]: rank q's shard of epoch e lands in staging[e & 1][q]
+// The shard (rows x row bytes, contiguous) is cut into `chunks` byte chunks (4 for decode shards,
+// up to 64 of ~256 KB for large ones; every rank derives the same count from the same size). A
+// call on rank r (epoch e, counted per (peer, chunk)) runs one CTA per (peer p, chunk c):
 //   * p == r: the CTA copies chunk c of r's own shard into r's block of Y;
 //   * p != r: the CTA stores chunk c of r's shard into p's staging[e & 1][r] (peer stores over
 //     NVLink), and after a CTA barrier one thread sets p's done[r][c] = e with a release store at
@@ -21,6 +22,7 @@
 // kErrPeerWait in the device error word (the results of that call are then undefined).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <new>
@@ -36,16 +38,17 @@ struct xrgpu_p2p {
   char* local = nullptr;
   char* peers[XRGPU_P2P_MAX_WORLD] = {};
   bool opened[XRGPU_P2P_MAX_WORLD] = {};
-  uint32_t* epoch = nullptr;  // device [XRGPU_P2P_MAX_WORLD * 4]: epoch of the last call, per (peer, chunk)
+  uint32_t* epoch = nullptr;  // device [XRGPU_P2P_MAX_WORLD * 64]: epoch of the last call, per (peer, chunk)
 };
 
 namespace xrgpu {
 namespace {
 
-constexpr int kFlagBytes = 256;
+constexpr int kMaxChunks = 64;                              // CTAs per peer at most
+constexpr int kFlagBytes = XRGPU_P2P_MAX_WORLD * kMaxChunks * 4;  // one done flag per (rank, chunk)
 constexpr int kThreads = 256;  // small enough to sit beside a running GEMV CTA
-constexpr int kChunks = 4;     // CTAs per peer: the peer stores of one shard spread over 4 SMs
-static_assert(XRGPU_P2P_MAX_WORLD * kChunks * 4 <= kFlagBytes, "done flags must fit the flag area");
+constexpr int kMinChunks = 4;  // CTAs per peer for small shards: the peer stores spread over 4 SMs
+constexpr int64_t kChunkBytes = 256 * 1024;  // target chunk size for large shards
 constexpr unsigned kErrPeerWait = 0x401;
 
 struct P2PParams {
@@ -54,7 +57,7 @@ struct P2PParams {
   const char* shard;  // [rows][srb]
   char* out;          // [rows][orb], rank q's block at byte q * srb, first ovb bytes of a row valid
   int64_t rows, srb, orb, ovb, slot_bytes;
-  int world, rank;
+  int world, rank, chunks;
   unsigned* err;
 };
 
@@ -94,9 +97,9 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
   // waits for this one); this kernel reads the shard only after the previous kernel completed.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int p = static_cast<int>(blockIdx.x) / kChunks, c = static_cast<int>(blockIdx.x) % kChunks;
+  const int p = static_cast<int>(blockIdx.x) / q.chunks, c = static_cast<int>(blockIdx.x) % q.chunks;
   const int64_t bytes = q.rows * q.srb;
-  const int64_t per = (bytes / 16 + kChunks - 1) / kChunks * 16;
+  const int64_t per = (bytes / 16 + q.chunks - 1) / q.chunks * 16;
   const int64_t lo = per * c < bytes ? per * c : bytes, hi = per * (c + 1) < bytes ? per * (c + 1) : bytes;
   const int64_t block_off = static_cast<int64_t>(p) * q.srb;
   const int64_t valid = q.ovb - block_off;
@@ -106,7 +109,7 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
   }
   __shared__ uint32_t epoch_s;
   __shared__ int ok_s;
-  uint32_t* epoch = q.epoch + p * kChunks + c;
+  uint32_t* epoch = q.epoch + p * kMaxChunks + c;
   if (threadIdx.x == 0) epoch_s = *epoch + 1u;
   __syncthreads();
   const uint32_t e = epoch_s;
@@ -120,8 +123,8 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
   __syncthreads();
   // 2. publish (release, system scope), then wait for p's chunk in this rank's staging
   if (threadIdx.x == 0) {
-    st_release_sys(reinterpret_cast<uint32_t*>(q.peers[p]) + q.rank * kChunks + c, e);
-    const uint32_t* mine = reinterpret_cast<const uint32_t*>(q.peers[q.rank]) + p * kChunks + c;
+    st_release_sys(reinterpret_cast<uint32_t*>(q.peers[p]) + q.rank * kMaxChunks + c, e);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(q.peers[q.rank]) + p * kMaxChunks + c;
     int ok = 1;
     if (static_cast<int32_t>(ld_acquire_sys(mine) - e) < 0) {
       const uint64_t start = global_timer_ns();
@@ -173,8 +176,8 @@ int xrgpu_p2p_create(int32_t device, int32_t world, int32_t rank, uint64_t slot_
     g->region_bytes = kFlagBytes + 2 * static_cast<uint64_t>(world) * g->slot_bytes;
     cudaIpcMemHandle_t h;
     if (cudaMalloc(&g->local, g->region_bytes) != cudaSuccess || cudaMemset(g->local, 0, g->region_bytes) != cudaSuccess ||
-        cudaMalloc(&g->epoch, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD * kChunks) != cudaSuccess ||
-        cudaMemset(g->epoch, 0, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD * kChunks) != cudaSuccess ||
+        cudaMalloc(&g->epoch, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD * kMaxChunks) != cudaSuccess ||
+        cudaMemset(g->epoch, 0, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD * kMaxChunks) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&h, g->local) != cudaSuccess) {
       st = api_fail(XRGPU_RUNTIME_ERROR, "peer-memory region allocation or IPC export failed");
     } else {
@@ -244,12 +247,14 @@ int xrgpu_p2p_allgather(xrgpu_p2p* g, const void* shard, int64_t rows, int64_t s
   q.slot_bytes = static_cast<int64_t>(g->slot_bytes);
   q.world = g->world;
   q.rank = g->rank;
+  const int64_t bytes = rows * shard_row_bytes;
+  q.chunks = static_cast<int>(std::min<int64_t>(kMaxChunks, std::max<int64_t>(kMinChunks, (bytes + kChunkBytes - 1) / kChunkBytes)));
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(g->device);
   q.err = device_error_word();
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(g->world * kChunks), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(g->world * q.chunks), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];

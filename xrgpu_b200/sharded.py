@@ -8,8 +8,8 @@ all-gather (NCCL over NVLink/NVSwitch) assembles Y. The reference backend is sin
 the contract (inputs, attributes, output shape and values) is unchanged.
 
 Shards are equal (``ceil(N / world)`` columns, the last one padded). On NCCL groups of one node,
-shards up to ``peer_max_bytes`` are exchanged by this package's peer-memory all-gather (one kernel
-over NVLink that writes Y directly, no NCCL call, so a step can be captured in a CUDA graph);
+shards up to ``peer_max_bytes`` (64 MB) are exchanged by this package's peer-memory all-gather (one
+kernel over NVLink that writes Y in place, no NCCL call, so a step can be captured in a CUDA graph);
 larger shards and gloo groups use ``all_gather_into_tensor`` / ``all_gather`` (for M == 1 the
 gathered buffer already is Y, for M > 1 one permute copy turns ``[world, M, S]`` into
 ``[M, world * S]``).
@@ -59,7 +59,7 @@ class ShardedMatMulNBits:
     def __init__(self, b: torch.Tensor, scales: torch.Tensor, zero_points: Optional[torch.Tensor] = None,
                  bias: Optional[torch.Tensor] = None, *, K: int, N: int, bits: int = 4, block_size: int,
                  group=None, compute: Optional[Callable] = None, peer_gather: Optional[bool] = None,
-                 peer_max_bytes: int = 4 << 20, peer_group=None, _presharded: bool = False):
+                 peer_max_bytes: int = 64 << 20, peer_group=None, _presharded: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
