@@ -88,6 +88,7 @@ class ShardedMatMulNBits:
         self._peer = None
         self._y_buf = None        # shard buffer of the overlapped form (see forward)
         self._gather_done = None  # event of the last overlapped gather
+
     @classmethod
     def from_shard(cls, b_shard: torch.Tensor, scales_shard: torch.Tensor, zero_points_shard=None, bias_shard=None,
                    *, K: int, N: int, bits: int = 4, block_size: int, group=None, compute=None, **kw):
