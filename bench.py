@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""MatMulNBits benchmark on B200: decode GB/s (and prefill TFLOP/s) through this repo's C ABI.
+"""MatMulNBits benchmark on B200: decode GB/s and prefill TFLOP/s through this repo's C ABI.
 
 Contract (one JSON line from rank 0):
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
@@ -18,11 +18,19 @@ Workloads (synthetic seeded data of their shapes/distribu
 Each step uses a different copy ("layer") of the weights; the copies total > 3x the 126 MB L2,
 so every step streams its weights from HBM (config: "l2": "rotating weight copies > L2").
 
-Multi-GPU (torchrun, one process per GPU, NCCL): every rank owns a contiguous 1/N slice of each
-projection's output columns (weak scaling: the model is N times wider, per-GPU work fixed) and the
-step ends with one all-gather of Y per projection: the library's peer-memory all-gather over NVLink
-for decode shards (the whole step is then one CUDA graph), NCCL for large prefill shards. Time is
-the max over ranks.
+The line for the default workload also carries a "prefill" object: config 4 (M=2048, K=4096,
+N=14336, bs 64, no zero points) measured in the same run with its own roofline, e2e and CPU
+baseline, so both halves of the metric are in one record.
+
+Multi-GPU (torchrun, one process per GPU, NCCL): the headline is weak scaling -- every rank owns a
+contiguous 1/N slice of each projection's output columns of an N-times-wider layer (per-GPU work
+fixed), and the step ends with one all-gather of Y per projection (the library's peer-memory
+all-gather over NVLink; NCCL for shards above 64 MB). Time is the max over ranks. The line adds
+  "strong": config 2 decode and config 4 prefill as FIXED problems sharded N ways (step time at N
+      GPUs, the same problem on one GPU, speed-up), each checked against the unsharded result;
+  "parity": the first step's gathered Y checked against a reference (strong problems: the
+      single-GPU kernel on the full problem, BASELINE tolerances; weak headline: an NCCL
+      all-gather of the same shards, bit-exact).
 
 --impl reference times the reference's own CPU algorithm (oracle/_ref: packedMatmul/nbitWeight
 compiled from the reference sources; the C oracle port when that is absent) on all host threads,
@@ -38,7 +46,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 import zlib
 from pathlib import Path
@@ -51,6 +58,9 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 LLAMA_LAYER = [("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
                ("gate", 4096, 14336), ("up", 4096, 14336), ("down", 14336, 4096)]
+# Dependencies of a decoder layer: q, k, v share their input; o needs attention over all three;
+# gate and up share their input; down needs both.
+LLAMA_GROUPS = [["q", "k", "v"], ["o"], ["gate", "up"], ["down"]]
 
 WORKLOADS = {
     "llama3_8b_decode": dict(config=2, M=1, bs=32, zp=True, scale=(0.005, 0.02), proj=LLAMA_LAYER, kind="decode"),
@@ -65,6 +75,7 @@ WORKLOADS = {
     "oracle_case": dict(config=1, M=1, bs=32, zp=False, scale=(0.005, 0.02), proj=[("proj", 4096, 4096)], kind="decode",
                         dtype="float32"),
 }
+TOL_MAX, TOL_FROB = 1e-2, 2e-3  # max|dY| <= 1e-2 max|Y_ref|, relative Frobenius <= 2e-3
 
 
 def log(*a):
@@ -78,10 +89,21 @@ def peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def proj_bytes(M, K, N, bs, zp, act_bytes):
+def proj_bytes(M, K, N, bs, zp, act_bytes, zp_bytes=None):
+    """Algorithmic bytes of one projection: B + scales + zero points + A + Y at their stored widths.
+    zp_bytes: bytes per zero point in the float form ([N, kb]); None = packed uint8 ([N, ceil(kb/2)])."""
     kb = K // bs
-    b = N * K // 2 + N * kb * act_bytes + (N * ((kb + 1) // 2) if zp else 0) + M * K * act_bytes + M * N * act_bytes
-    return b
+    z = 0
+    if zp:
+        z = N * kb * zp_bytes if zp_bytes else N * ((kb + 1) // 2)
+    return N * K // 2 + N * kb * act_bytes + z + M * K * act_bytes + M * N * act_bytes
+
+
+def groups_for(wl):
+    names = [n for (n, _, _) in wl["proj"]]
+    if sorted(names) == sorted(n for g in LLAMA_GROUPS for n in g):
+        return [list(g) for g in LLAMA_GROUPS]
+    return [[n] for n in names]  # other workloads: each projection depends on the last
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -128,18 +150,19 @@ class ClockSampler:
             pass
         if not rows:
             return out
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        num = lambda v: v.replace(".", "").isdigit()  # noqa: E731
+        sm = [float(r[1]) for r in rows if num(r[1])]
+        mx = [float(r[2]) for r in rows if num(r[2])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        power = [float(r[3]) for r in rows if num(r[3])]
         out.update(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=max(mx) if mx else None,
-                   reasons=reasons, samples=len(rows),
-                   power_w_max=max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit()) if rows else None)
+                   reasons=reasons, samples=len(rows), power_w_max=max(power) if power else None)
         return out
 
 
 # ----------------------------------------------------------------------------- distributed
-def dist_init(n_gpus):
+def dist_init():
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -155,11 +178,11 @@ def dist_init(n_gpus):
 
 
 def barrier(world):
+    import torch
     if world > 1:
-        import torch
         import torch.distributed as dist
         dist.barrier()
-        torch.cuda.synchronize()
+    torch.cuda.synchronize()
 
 
 def max_over_ranks(world, value):
@@ -172,194 +195,225 @@ def max_over_ranks(world, value):
     return float(t.item())
 
 
+def min_over_ranks(world, value):
+    return -max_over_ranks(world, -value)
+
+
 # ----------------------------------------------------------------------------- data
-def make_weights(wl, world, rank, layers, seed, device):
-    """Per layer and projection: this rank's column shard of B, scales, zero points."""
+def seed_of(seed, layer, name, rank):
+    return seed * 1000003 + layer * 1009 + zlib.crc32(name.encode()) % 997 + 7919 * rank
+
+
+def gen_projection(wl, name, K, N, key, device, dtype):
+    """B, scales and (packed) zero points of one projection, seeded by `key` (BASELINE distributions)."""
     import torch
     g = torch.Generator(device=device)
-    out = []
+    g.manual_seed(key)
+    kb = K // wl["bs"]
     lo, hi = wl["scale"]
-    for layer in range(layers):
-        projs = []
-        for (name, K, N) in wl["proj"]:
-            n_local = N  # weak scaling: each rank owns N columns of an N*world-wide projection
-            g.manual_seed(seed * 1000003 + layer * 1009 + zlib.crc32(name.encode()) % 997 + 7919 * rank)
-            kb = K // wl["bs"]
-            b = torch.randint(0, 256, (n_local, kb, wl["bs"] // 2), dtype=torch.uint8, device=device, generator=g)
-            s = (torch.rand((n_local, kb), device=device, generator=g) * (hi - lo) + lo).to(torch.float16)
-            zp = (torch.randint(0, 256, (n_local, (kb + 1) // 2), dtype=torch.uint8, device=device, generator=g)
-                  if wl["zp"] else None)
-            projs.append(dict(name=name, K=K, N=n_local, b=b, s=s, zp=zp))
-        out.append(projs)
-    return out
+    b = torch.randint(0, 256, (N, kb, wl["bs"] // 2), dtype=torch.uint8, device=device, generator=g)
+    s = (torch.rand((N, kb), device=device, generator=g) * (hi - lo) + lo).to(torch.float16).to(dtype)
+    zp = torch.randint(0, 256, (N, (kb + 1) // 2), dtype=torch.uint8, device=device, generator=g) if wl["zp"] else None
+    return dict(name=name, K=K, N=N, b=b, s=s, zp=zp)
 
 
-def layers_for_l2(wl, l2_bytes):
-    per_layer = sum(proj_bytes(wl["M"], K, N, wl["bs"], wl["zp"], 2) for (_, K, N) in wl["proj"])
-    return max(2, math.ceil(3 * l2_bytes / per_layer) + 1), per_layer
+def within_tol(got, ref):
+    """(ok, max|dY| / max|Y_ref|, relative Frobenius) under BASELINE.json's tolerances."""
+    d = (got.double() - ref.double())
+    scale = ref.double().abs().max().item()
+    rel_max = d.abs().max().item() / max(scale, 1e-30)
+    frob = (d.norm() / ref.double().norm().clamp_min(1e-30)).item()
+    return rel_max <= TOL_MAX and frob <= TOL_FROB, rel_max, frob
 
 
-# ----------------------------------------------------------------------------- our arm
-def run_ours(args, wl):
-    import torch
-    from xrgpu_b200 import functional as F
-    from xrgpu_b200 import _native
+class Runner:
+    """One workload's decode or prefill step on this rank.
 
-    world, rank, local = dist_init(args.gpus)
-    lib = _native.load()
-    device = torch.device("cuda", local)
-    props = torch.cuda.get_device_properties(device)
-    l2 = getattr(props, "L2_cache_size", 126 * 2**20) or 126 * 2**20
-    layers, per_layer = layers_for_l2(wl, l2)
-    if args.layers:
-        layers = args.layers
-    M = wl["M"]
-    dt = torch.float32 if wl.get("dtype") == "float32" else torch.float16
-    act_bytes = 4 if dt == torch.float32 else 2
-    weights = make_weights(wl, world, rank, layers, args.seed, device)
-    if dt == torch.float32:
-        for layer in weights:
-            for p in layer:
-                p["s"] = p["s"].float()
-    g = torch.Generator(device=device)
-    g.manual_seed(args.seed)
-    acts = {K: torch.randn((M, K), generator=g, device=device, dtype=torch.float32).to(dt)
-            for K in sorted({K for (_, K, _) in wl["proj"]})}
-    ys = {(name, N): torch.empty((M, N), device=device, dtype=dt) for (name, K, N) in wl["proj"]}
-    gathered = {(name, N): torch.empty((M, N * world), device=device, dtype=dt) for (name, K, N) in wl["proj"]}
-    launches_per_step = len(wl["proj"])
-    paths = sorted({F.select_path(acts[p["K"]], p["b"], p["s"], p["zp"], K=p["K"], N=p["N"], block_size=wl["bs"])
-                    for p in weights[0]})
+    mode "weak": this rank owns N columns of an (N * world)-wide projection (its own seeded shard).
+    mode "strong": every rank generates the same full projection and keeps its 1/world column slice
+    (ShardedMatMulNBits); the first `keep_full` layers keep the full weights for the single-GPU
+    comparison. With world == 1 a step is plain ``functional.matmul_nbits`` calls.
+    """
 
-    shared = None
-    if world > 1:
-        # Each rank's shard is one column slice of an (N * world)-wide projection, used through the
-        # library's sharded module: local kernel + one all-gather of Y per projection (peer memory
-        # for small shards, NCCL otherwise).
-        from xrgpu_b200.sharded import ShardedMatMulNBits
-        from xrgpu_b200.p2p import PeerAllGather
-        for layer in weights:
-            for p in layer:
-                p["mod"] = ShardedMatMulNBits.from_shard(p["b"], p["s"], p["zp"], None, K=p["K"], N=p["N"] * world,
-                                                         block_size=wl["bs"])
-        if all(p["mod"].uses_peer_gather(M) for layer in weights for p in layer):
-            # one peer-memory group shared by every projection (calls are stream-ordered)
-            shared = PeerAllGather(max(M * p["N"] * 2 for p in weights[0]))
-            for layer in weights:
+    def __init__(self, wl, args, world, rank, device, mode="weak", max_layers=64):
+        import torch
+        from xrgpu_b200 import functional as F
+        self.F = F
+        self.wl, self.args, self.world, self.rank, self.device, self.mode = wl, args, world, rank, device, mode
+        self.M = wl["M"]
+        self.dt = torch.float32 if wl.get("dtype") == "float32" else torch.float16
+        self.act_bytes = 4 if self.dt == torch.float32 else 2
+        props = torch.cuda.get_device_properties(device)
+        l2 = getattr(props, "L2_cache_size", 126 * 2**20) or 126 * 2**20
+        # bytes this rank streams per step, and the whole job's algorithmic bytes / FLOPs per step
+        if mode == "weak":
+            self.rank_proj = [(n, K, N) for (n, K, N) in wl["proj"]]
+            self.full_proj = [(n, K, N * world) for (n, K, N) in wl["proj"]]
+        else:
+            self.full_proj = [(n, K, N) for (n, K, N) in wl["proj"]]
+            self.rank_proj = [(n, K, -(-N // world)) for (n, K, N) in wl["proj"]]
+        pb = lambda projs: sum(proj_bytes(self.M, K, N, wl["bs"], wl["zp"], self.act_bytes) for (_, K, N) in projs)  # noqa: E731
+        self.bytes_rank, self.bytes_job = pb(self.rank_proj), pb(self.full_proj)
+        self.flops_job = sum(2 * self.M * K * N for (_, K, N) in self.full_proj)
+        self.layers = args.layers or min(max_layers, max(2, math.ceil(3 * l2 / self.bytes_rank) + 1))
+        self.groups = groups_for(wl)
+        self.keep_full = 0
+        self._build()
+
+    def _build(self):
+        import torch
+        wl, dev, F = self.wl, self.device, self.F
+        g = torch.Generator(device=dev)
+        g.manual_seed(self.args.seed)
+        self.acts = {K: torch.randn((self.M, K), generator=g, device=dev, dtype=torch.float32).to(self.dt)
+                     for K in sorted({K for (_, K, _) in wl["proj"]})}
+        self.ys = {n: torch.empty((self.M, N), device=dev, dtype=self.dt) for (n, K, N) in self.full_proj}
+        self.weights, self.full = [], []
+        self.keep_full = min(self.layers, 4) if (self.mode == "strong" and self.world > 1) else 0
+        shared_bytes = 0
+        for layer in range(self.layers):
+            projs = []
+            for (name, K, N) in wl["proj"]:
+                if self.mode == "weak":
+                    p = gen_projection(wl, name, K, N, seed_of(self.args.seed, layer, name, self.rank), dev, self.dt)
+                else:
+                    p = gen_projection(wl, name, K, N, seed_of(self.args.seed, layer, name, 0), dev, self.dt)
+                projs.append(p)
+            if self.world > 1:
+                from xrgpu_b200.sharded import ShardedMatMulNBits
+                mods = []
+                for p, (name, K, Nf) in zip(projs, self.full_proj):
+                    if self.mode == "weak":
+                        mod = ShardedMatMulNBits.from_shard(p["b"], p["s"], p["zp"], None, K=K, N=Nf, block_size=wl["bs"])
+                    else:
+                        mod = ShardedMatMulNBits(p["b"], p["s"], p["zp"], None, K=K, N=Nf, block_size=wl["bs"])
+                    shared_bytes = max(shared_bytes, self.M * mod.S * self.act_bytes)
+                    mods.append(dict(name=name, K=K, N=Nf, mod=mod))
+                if layer < self.keep_full:
+                    self.full.append(projs)  # full weights of this layer, for the single-GPU comparison
+                projs = mods
+            self.weights.append(projs)
+        self.paths = sorted({self._path(K, N) for (_, K, N) in self.rank_proj})
+        self.shared = None
+        self.peer = self.world > 1 and all(p["mod"].uses_peer_gather(self.M, self.act_bytes)
+                                           for layer in self.weights for p in layer)
+        if self.peer:
+            from xrgpu_b200.p2p import PeerAllGather
+            # one peer-memory group shared by every projection (calls are stream-ordered), created
+            # before any capture
+            self.shared = PeerAllGather(shared_bytes)
+            for layer in self.weights:
                 for p in layer:
-                    p["mod"].set_peer_group(shared)
+                    p["mod"].set_peer_group(self.shared)
+        self.overlap = self.peer and not self.args.no_overlap
+        self.comm = torch.cuda.Stream(dev) if self.overlap else None
+        self.graphs = []
 
-    # With N > 1 ranks and peer-memory all-gathers, a projection's all-gather may overlap the GEMVs
-    # that do not depend on its Y: in a decoder layer q, k, v share their input, o needs attention
-    # over all three, gate and up share their input and down needs both. Each group's gathers are
-    # joined before the next group starts, so the gathers of v, o, up and down stay exposed.
-    order = [p["name"] for p in weights[0]]
-    layer_groups = [["q", "k", "v"], ["o"], ["gate", "up"], ["down"]]
-    if sorted(order) != sorted(n for grp in layer_groups for n in grp):
-        layer_groups = [[n] for n in order]  # other workloads: each projection depends on the last
-    overlap = world > 1 and shared is not None and not args.no_overlap
-    comm = torch.cuda.Stream(device) if overlap else None
+    def _path(self, K, N):
+        import torch
+        dev = self.device
+        kb = K // self.wl["bs"]
+        b = torch.empty((N, kb, self.wl["bs"] // 2), dtype=torch.uint8, device=dev)
+        s = torch.empty((N, kb), dtype=self.dt, device=dev)
+        zp = torch.empty((N, (kb + 1) // 2), dtype=torch.uint8, device=dev) if self.wl["zp"] else None
+        return self.F.select_path(self.acts[K], b, s, zp, K=K, N=N, block_size=self.wl["bs"])
 
-    def step(layer, gather=True):
-        by_name = {p["name"]: p for p in weights[layer]}
-        if world > 1 and gather and overlap:
-            for grp in layer_groups:
+    # ------------------------------------------------------------------ execution
+    def step(self, layer):
+        """One step over layer `layer`: the projections in dependency-group order."""
+        projs = {p["name"]: p for p in self.weights[layer]}
+        bs = self.wl["bs"]
+        for grp in self.groups:
+            for name in grp:
+                p = projs[name]
+                x = self.acts[p["K"]]
+                if self.world == 1:
+                    self.F.matmul_nbits(x, p["b"], p["s"], p["zp"], K=p["K"], N=p["N"], block_size=bs, out=self.ys[name])
+                elif self.overlap:  # the gather runs beside the group's other kernels
+                    p["mod"](x, out=self.ys[name], gather_stream=self.comm)
+                else:
+                    p["mod"](x, out=self.ys[name])
+            if self.world > 1 and self.overlap:
                 for name in grp:
-                    p = by_name[name]
-                    p["mod"](acts[p["K"]], out=gathered[(p["name"], p["N"])], gather_stream=comm)
-                for name in grp:
-                    by_name[name]["mod"].wait_gather()
-            return
-        for p in weights[layer]:
-            if world > 1 and gather:
-                p["mod"](acts[p["K"]], out=gathered[(p["name"], p["N"])])
-            else:
-                y = ys[(p["name"], p["N"])]
-                F.matmul_nbits(acts[p["K"]], p["b"], p["s"], p["zp"], K=p["K"], N=p["N"], block_size=wl["bs"], out=y)
+                    projs[name]["mod"].wait_gather()
 
-    # Warm-up outside capture (allocates the library workspace, sets kernel attributes).
-    for layer in range(layers):
-        step(layer)
-    torch.cuda.synchronize()
-    # Each layer's step is one CUDA graph when it contains no NCCL call: always on one GPU, and with
-    # N > 1 ranks when every projection's all-gather goes through peer memory. Steps that hold NCCL
-    # all-gathers run eagerly.
-    peer = world > 1 and all(p["mod"].uses_peer_gather(M) for layer in weights for p in layer)
-    use_graphs = (world == 1 or peer) and not args.no_graphs
-    graphs = []
-    if use_graphs:
-        stream = torch.cuda.Stream(device)
-        with torch.cuda.stream(stream):
-            for layer in range(layers):
-                gr = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gr, stream=stream):
-                    step(layer)
-                graphs.append(gr)
+    def step_full(self, layer):
+        """The unsharded problem of a kept layer on this GPU alone (strong-scaling comparison)."""
+        for p in self.full[layer]:
+            self.F.matmul_nbits(self.acts[p["K"]], p["b"], p["s"], p["zp"], K=p["K"], N=p["N"],
+                                block_size=self.wl["bs"], out=self.ys_full[p["name"]])
+
+    @property
+    def graphable(self):
+        return (self.world == 1 or self.peer) and not self.args.no_graphs
+
+    def capture(self, fn, count):
+        """One CUDA graph per layer of fn(layer) (only for steps without NCCL calls)."""
+        import torch
+        graphs = []
+        s = torch.cuda.Stream(self.device)
+        with torch.cuda.stream(s):
+            for layer in range(count):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    fn(layer)
+                graphs.append(g)
         torch.cuda.synchronize()
+        return graphs
 
-    def run_steps(n, offset=0):
-        for i in range(n):
-            layer = (offset + i) % layers
-            if use_graphs:
-                graphs[layer].replay()
-            else:
-                step(layer)
+    def timed(self, fn, count, graphs, steps, warmup, clocks=None):
+        """Device time per step (ms, max over ranks) of `steps` steps after `warmup` untimed ones,
+        bracketed by a barrier and a synchronize on both sides."""
+        import torch
 
-    log(f"[rank {rank}] graphs captured: {len(graphs)}")
-    run_steps(max(3, args.warmup))
-    log(f"[rank {rank}] warm-up done")
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    barrier(world)
-    clocks.start()
-    time.sleep(0.25)
-    torch.cuda.synchronize()
-    barrier(world)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    run_steps(args.steps)
-    t1.record()
-    torch.cuda.synchronize()
-    barrier(world)
-    ms_local = t0.elapsed_time(t1)
-    # The max over ranks is taken before anything depends on it: every rank must then run the
-    # same number of extra steps (each holds collectives).
-    ms = max_over_ranks(world, ms_local)
-    # Keep the clock sampler running for at least a few samples.
-    if ms < 600:
-        reps = max(1, int(600 / max(ms, 1e-3)))
-        for _ in range(reps):
-            run_steps(args.steps)
+        def run(n, offset=0):
+            for i in range(n):
+                layer = (offset + i) % count
+                if graphs:
+                    graphs[layer].replay()
+                else:
+                    fn(layer)
+
+        run(max(3, warmup))
+        barrier(self.world)
+        if clocks is not None:
+            clocks.start()
+            time.sleep(0.25)
+        barrier(self.world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        run(steps)
+        t1.record()
         torch.cuda.synchronize()
-    clock = clocks.stop()
-    step_ms = ms / args.steps
-    bytes_rank = per_layer if wl["kind"] == "decode" else None
-    flops_rank = sum(2 * M * K * N for (_, K, N) in wl["proj"])
-    pk, pk_kind = peaks()
-    result = {}
-    if wl["kind"] == "decode":
-        value = bytes_rank * world / (step_ms * 1e-3) / 1e9
-        metric, unit = "MatMulNBits decode GB/s", "GB/s"
-    else:
-        value = flops_rank * world / (step_ms * 1e-3) / 1e12
-        metric, unit = "MatMulNBits prefill TFLOP/s", "TFLOP/s"
+        barrier(self.world)
+        ms = max_over_ranks(self.world, t0.elapsed_time(t1))
+        clock = None
+        if clocks is not None:
+            # keep the sampler running for a few samples: every rank runs the same extra steps
+            # (ms is the same on every rank after the max)
+            reps = max(1, int(600 / max(ms, 1e-3))) if ms < 600 else 0
+            for _ in range(reps):
+                run(steps)
+            torch.cuda.synchronize()
+            clock = clocks.stop()
+        return ms / steps, clock
 
-    # Each projection's kernel alone: a CUDA graph of back-to-back launches over the rotating
-    # weight copies (no host launch overhead between them).
-    kernel = {}
-    # Per-projection kernel times: one GPU only (no collectives inside; with several ranks one
-    # rank capturing graphs while the others sit in collectives would only add waiting).
-    if world == 1:
-        for (name, K, N) in wl["proj"]:
-            reps = 4 * layers
-            gs = torch.cuda.Stream(device)
+    def kernel_times(self):
+        """Each projection alone: a CUDA graph of back-to-back launches over the rotating copies
+        (one GPU only)."""
+        import torch
+        out = {}
+        bs = self.wl["bs"]
+        for (name, K, N) in self.rank_proj:
+            reps = 4 * self.layers
+            gs = torch.cuda.Stream(self.device)
             gk = torch.cuda.CUDAGraph()
             with torch.cuda.stream(gs):
                 with torch.cuda.graph(gk, stream=gs):
                     for r in range(reps):
-                        p = [q for q in weights[r % layers] if q["name"] == name][0]
-                        F.matmul_nbits(acts[K], p["b"], p["s"], p["zp"], K=K, N=N, block_size=wl["bs"],
-                                       out=ys[(name, N)])
+                        p = [q for q in self.weights[r % self.layers] if q["name"] == name][0]
+                        self.F.matmul_nbits(self.acts[K], p["b"], p["s"], p["zp"], K=K, N=N, block_size=bs,
+                                            out=self.ys[name])
             torch.cuda.synchronize()
             gk.replay()
             torch.cuda.synchronize()
@@ -370,98 +424,241 @@ def run_ours(args, wl):
             ev1.record()
             torch.cuda.synchronize()
             per = ev0.elapsed_time(ev1) / (5 * reps)
-            kb = proj_bytes(M, K, N, wl["bs"], wl["zp"], act_bytes)
-            kernel[name] = dict(K=K, N=N, us=round(per * 1e3, 3), gbs=round(kb / (per * 1e-3) / 1e9, 1),
-                                tflops=round(2 * M * K * N / (per * 1e-3) / 1e12, 3))
+            kb = proj_bytes(self.M, K, N, bs, self.wl["zp"], self.act_bytes)
+            out[name] = dict(K=K, N=N, us=round(per * 1e3, 3), gbs=round(kb / (per * 1e-3) / 1e9, 1),
+                             tflops=round(2 * self.M * K * N / (per * 1e-3) / 1e12, 3))
             del gk
+        return out
+
+    def value_of(self, ms):
+        if self.wl["kind"] == "decode":
+            return self.bytes_job / (ms * 1e-3) / 1e9
+        return self.flops_job / (ms * 1e-3) / 1e12
+
+    def e2e(self, steps, warmup):
+        """End to end through the public call: every step copies its activations in from pinned host
+        memory, runs the step's library calls and copies every Y out to pinned host memory, then
+        synchronises. Steps without NCCL calls replay one CUDA graph holding the copies and the calls
+        (recorded through the same public API); the eager form is timed too (e2e_eager_ms)."""
+        import torch
+        host_a = {K: a.cpu().pin_memory() for K, a in self.acts.items()}
+        host_y = {n: torch.empty(y.shape, dtype=y.dtype).pin_memory() for n, y in self.ys.items()}
+        h2d = sum(v.numel() * v.element_size() for v in host_a.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_y.values())
+
+        def body(layer):
+            for K, h in host_a.items():
+                self.acts[K].copy_(h, non_blocking=True)
+            self.step(layer)
+            for n, h in host_y.items():
+                h.copy_(self.ys[n], non_blocking=True)
+
+        def timed_e2e(graphs):
+            for i in range(max(3, warmup)):
+                graphs[i % len(graphs)].replay() if graphs else body(i % self.layers)
+                torch.cuda.synchronize()
+            barrier(self.world)
+            w0 = time.perf_counter()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(steps):
+                if graphs:
+                    graphs[i % len(graphs)].replay()
+                else:
+                    body(i % self.layers)
+                torch.cuda.synchronize()
+            e1.record()
+            torch.cuda.synchronize()
+            wall = time.perf_counter() - w0
+            return max_over_ranks(self.world, max(e0.elapsed_time(e1), wall * 1e3) / steps)
+
+        eager_ms = timed_e2e(None)
+        graphs = self.capture(body, self.layers) if self.graphable else None
+        e_ms = timed_e2e(graphs) if graphs else eager_ms
+        del graphs
+        unit = "GB/s" if self.wl["kind"] == "decode" else "TFLOP/s"
+        api = "functional.matmul_nbits -> xrgpu_mmnb_forward (C ABI)"
+        if self.world > 1:
+            api = "ShardedMatMulNBits -> " + api + " + peer-memory all-gather"
+        return dict(value=round(self.value_of(e_ms), 2), unit=unit, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                    ms_per_step=round(e_ms, 4), e2e_eager_ms=round(eager_ms, 4),
+                    path=api + ("; one CUDA graph per step holding the host copies and the calls, one sync per step"
+                                if self.graphable else "; eager calls, one sync per step"))
+
+    # ------------------------------------------------------------------ checks
+    def parity(self):
+        """Check the first step's gathered Y (world > 1). strong: against the single-GPU kernel on the
+        full problem (BASELINE tolerances); weak: against an NCCL all-gather of the same shards
+        (bit-exact). Every rank checks; the verdict is the AND over ranks."""
+        import torch
+        import torch.distributed as dist
+        self.step(0)
+        torch.cuda.synchronize()
+        ok, worst_max, worst_frob = True, 0.0, 0.0
+        if self.mode == "strong":
+            self.ys_full = {n: torch.empty_like(y) for n, y in self.ys.items()}
+            self.step_full(0)
+            torch.cuda.synchronize()
+            for n in self.ys:
+                good, rel_max, frob = within_tol(self.ys[n], self.ys_full[n])
+                ok &= good
+                worst_max, worst_frob = max(worst_max, rel_max), max(worst_frob, frob)
+            kind = "gathered Y vs the single-GPU kernel on the full problem (BASELINE tolerances)"
+        else:
+            for p in self.weights[0]:
+                mod, n = p["mod"], p["name"]
+                y_local = torch.empty((self.M, mod.S), dtype=self.dt, device=self.device)
+                mod.local(self.acts[p["K"]], y_local)
+                g = torch.empty((self.world, self.M, mod.S), dtype=self.dt, device=self.device)
+                dist.all_gather_into_tensor(g, y_local)
+                ref = g.permute(1, 0, 2).reshape(self.M, self.world * mod.S)[:, :p["N"]]
+                ok &= torch.equal(self.ys[n], ref)
+            kind = "gathered Y vs an NCCL all-gather of the same shards (bit-exact)"
+        ok = min_over_ranks(self.world, 1.0 if ok else 0.0) > 0.5
+        out = dict(ok=bool(ok), check=kind, ranks=self.world, projections=[n for (n, _, _) in self.full_proj])
+        if self.mode == "strong":
+            out.update(max_rel=float(f"{max_over_ranks(self.world, worst_max):.3e}"),
+                       rel_frobenius=float(f"{max_over_ranks(self.world, worst_frob):.3e}"), tol_max=TOL_MAX,
+                       tol_frobenius=TOL_FROB)
+        return out
+
+    def close(self):
+        self.graphs = []
+        if self.world > 1:
+            import torch
+            torch.cuda.synchronize()
+            for layer in self.weights:
+                for p in layer:
+                    p["mod"].close()
+            if self.shared is not None:
+                self.shared.close()  # collective: every rank closes it at the same point
+
+
+def roofline_of(runner, step_ms, pk, pk_kind):
+    wl = runner.wl
     if wl["kind"] == "decode":
-        achieved = bytes_rank / (step_ms * 1e-3) / 1e9
+        achieved = runner.bytes_rank / (step_ms * 1e-3) / 1e9
         peak = pk["hbm_gbs"]
-        roofline = dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s", frac=round(achieved / peak, 4),
-                        traffic=None, peak_source=f"{pk_kind} hbm_gbs",
-                        note="achieved = algorithmic bytes per step / device time per step (CUDA graph of the step's "
-                             "launches, rotating weight copies); per-projection kernel times in kernels_us")
+        r = dict(bound="hbm", achieved=round(achieved, 1), peak=peak, unit="GB/s", frac=round(achieved / peak, 4),
+                 traffic=None, peak_source=f"{pk_kind} hbm_gbs",
+                 note="achieved = algorithmic bytes this GPU streams per step / device time per step (CUDA graph "
+                      "of the step's launches, rotating weight copies); per-projection kernel times in kernels_us")
     else:
+        flops_rank = sum(2 * runner.M * K * N for (_, K, N) in runner.rank_proj)
         achieved = flops_rank / (step_ms * 1e-3) / 1e12
         peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
-        roofline = dict(bound="tensor", achieved=round(achieved, 1), peak=peak, unit="TFLOP/s",
-                        frac=round(achieved / peak, 4), traffic=None, peak_source=f"{pk_kind} bf16_tflops (burst)")
+        r = dict(bound="tensor", achieved=round(achieved, 1), peak=peak, unit="TFLOP/s", frac=round(achieved / peak, 4),
+                 traffic=None, peak_source=f"{pk_kind} bf16_tflops (burst: the GEMM is timed alone)")
+    return r
+
+
+def attach_traffic(roofline, workload):
     traffic_file = ROOT / "profiles" / "traffic.json"
     if traffic_file.exists():
-        tr = json.loads(traffic_file.read_text()).get(args.workload)
+        tr = json.loads(traffic_file.read_text()).get(workload)
         if tr:
             roofline["traffic"] = tr.get("bytes_per_step")
             roofline["traffic_source"] = tr.get("source")
 
-    log(f"[rank {rank}] timed region done")
-    # End to end through the public C-ABI call: pinned host A -> device, the step's C-ABI calls,
-    # device -> pinned host Y, synchronise; every step.
-    e2e = None
-    if not args.no_e2e:
-        host_a = {K: acts[K].cpu().pin_memory() for K in acts}
-        host_y = {key: torch.empty_like(v, device="cpu").pin_memory() for key, v in
-                  (gathered.items() if world > 1 else ys.items())}
-        h2d = sum(v.numel() * v.element_size() for v in host_a.values())
-        d2h = sum(v.numel() * v.element_size() for v in host_y.values())
 
-        def e2e_step(i):
-            for K, h in host_a.items():
-                acts[K].copy_(h, non_blocking=True)
-            step(i % layers)
-            src = gathered if world > 1 else ys
-            for key, h in host_y.items():
-                h.copy_(src[key], non_blocking=True)
-            torch.cuda.synchronize()
+# ----------------------------------------------------------------------------- our arm
+def measure(name, args, world, rank, local, device, *, mode="weak", headline=False, cpu=False):
+    """Time one workload; returns the pieces of a JSON line (rank 0 uses them)."""
+    wl = WORKLOADS[name]
+    pk, pk_kind = peaks()
+    runner = Runner(wl, args, world, rank, device, mode=mode, max_layers=64 if wl["kind"] == "decode" else 16)
+    log(f"[rank {rank}] {name} ({mode}): {runner.layers} weight copies, paths {runner.paths}")
+    for layer in range(runner.layers):  # warm-up outside capture (kernel attributes, peer group)
+        runner.step(layer)
+    import torch
+    torch.cuda.synchronize()
+    res = dict(workload=name, config=wl["config"], mode=mode, layers=runner.layers, paths=runner.paths)
+    if world > 1:
+        res["parity"] = runner.parity()
+    graphs = runner.capture(runner.step, runner.layers) if runner.graphable else None
+    clocks = ClockSampler(local) if headline else None
+    step_ms, clock = runner.timed(runner.step, runner.layers, graphs, args.steps, args.warmup, clocks)
+    del graphs
+    res.update(step_ms=step_ms, value=runner.value_of(step_ms), clocks=clock,
+               unit="GB/s" if wl["kind"] == "decode" else "TFLOP/s",
+               metric="MatMulNBits decode GB/s" if wl["kind"] == "decode" else "MatMulNBits prefill TFLOP/s",
+               roofline=roofline_of(runner, step_ms, pk, pk_kind), graphs=runner.graphable,
+               overlap=runner.overlap, peer=runner.peer, launches=len(wl["proj"]))
+    attach_traffic(res["roofline"], name)
+    if world == 1:
+        res["kernels_us"] = runner.kernel_times()
+    if mode == "strong" and world > 1:
+        runner.ys_full = {n: torch.empty_like(y) for n, y in runner.ys.items()}
+        g1 = runner.capture(runner.step_full, len(runner.full)) if not args.no_graphs else None
+        one_ms, _ = runner.timed(runner.step_full, len(runner.full), g1, args.steps, args.warmup)
+        del g1
+        res.update(one_gpu_ms=one_ms, speedup=one_ms / step_ms, efficiency=one_ms / step_ms / world)
+    if not args.no_e2e and mode == "weak":
+        res["e2e"] = runner.e2e(args.steps, args.warmup)
+    if cpu and rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_reference_time(wl, budget_s=args.cpu_seconds, kind_pref="reference")
+    runner.close()
+    del runner
+    torch.cuda.empty_cache()
+    return res
 
-        for i in range(max(3, args.warmup)):
-            e2e_step(i)
-        barrier(world)
-        w0 = time.perf_counter()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(args.steps):
-            e2e_step(i)
-        e1.record()
-        torch.cuda.synchronize()
-        wall = time.perf_counter() - w0
-        e_ms = max_over_ranks(world, max(e0.elapsed_time(e1), wall * 1e3) / args.steps)
-        e_val = (bytes_rank * world / (e_ms * 1e-3) / 1e9) if wl["kind"] == "decode" else (flops_rank * world / (e_ms * 1e-3) / 1e12)
-        e2e = dict(value=round(e_val, 2), unit=unit, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h, ms_per_step=round(e_ms, 4),
-                   path=("ShardedMatMulNBits -> " if world > 1 else "") +
-                   "functional.matmul_nbits -> xrgpu_mmnb_forward (C ABI), one sync per step")
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_reference_time(wl, budget_s=args.cpu_seconds, kind_pref="reference")
+def run_ours(args):
+    import torch
+    from xrgpu_b200 import _native
 
+    world, rank, local = dist_init()
+    _native.load()
+    device = torch.device("cuda", local)
+    head = measure(args.workload, args, world, rank, local, device, mode="weak", headline=True, cpu=True)
+    wl = WORKLOADS[args.workload]
+    extra = {}
+    if args.workload == "llama3_8b_decode" and not args.no_prefill:
+        pre = measure("prefill_m2048", args, world, rank, local, device, mode="weak", cpu=True)
+        extra["prefill"] = {k: pre[k] for k in ("metric", "unit", "config", "paths", "layers", "roofline", "graphs")
+                            if k in pre}
+        extra["prefill"].update(value=round(pre["value"], 2), ms_per_step=round(pre["step_ms"], 5),
+                                workload="prefill_m2048", M=2048, K=4096, N=14336, block_size=64, zero_points="none",
+                                e2e=pre.get("e2e"), cpu_baseline=pre.get("cpu_baseline"),
+                                kernels_us=pre.get("kernels_us"), parity=pre.get("parity"))
+    if world > 1 and not args.no_strong:
+        strong = {}
+        for name in ("llama3_8b_decode", "prefill_m2048"):
+            r = measure(name, args, world, rank, local, device, mode="strong")
+            strong[name] = dict(unit=r["unit"], value=round(r["value"], 2), ms_per_step=round(r["step_ms"], 5),
+                                one_gpu_ms_per_step=round(r["one_gpu_ms"], 5), speedup=round(r["speedup"], 3),
+                                parallel_efficiency=round(r["efficiency"], 3), parity=r["parity"],
+                                roofline_per_gpu=r["roofline"], graphs=r["graphs"])
+        extra["strong"] = strong
     if world > 1:
         import torch.distributed as dist
-        graphs.clear()  # graphs are released before the process group goes
-        torch.cuda.synchronize()
-        for layer in weights:
-            for p in layer:
-                p["mod"].close()
-        if shared is not None:
-            shared.close()  # collective: every rank closes it at the same point
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
+    step_ms = head["step_ms"]
+    dt = "fp32" if wl.get("dtype") == "float32" else "fp16 activations x 4-bit weights, fp32 accumulate"
+    proj = wl["proj"] if world == 1 else [[n, K, N * world] for (n, K, N) in wl["proj"]]
     line = {
-        "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp16 activations x 4-bit weights, fp32 accumulate" if dt == torch.float16 else "fp32",
+        "metric": head["metric"], "value": round(head["value"], 2), "unit": head["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": dt,
         "data": "synthetic (seeded torch RNG; BASELINE.json distributions)",
-        "config": {"workload": args.workload, "baseline_config": wl["config"], "M": M,
-                   "projections": [[n, K, N] for (n, K, N) in wl["proj"]], "bits": 4, "block_size": wl["bs"],
-                   "zero_points": "packed uint8" if wl["zp"] else "none", "l2": f"{layers} rotating weight copies "
-                   f"({layers * per_layer / 1e6:.0f} MB > 3x L2)", "parallelism": f"column-shard x{world}" +
-                   ((" + peer-memory all-gather of Y" + (" overlapped within q/k/v and gate/up" if overlap and any(len(g) > 1 for g in layer_groups) else "")
-                    if peer else " + NCCL all-gather of Y") if world > 1 else ""),
-                   "cuda_graphs": use_graphs, "paths": paths},
-        "roofline": roofline, "kernels_us": kernel, "gpu_launches": launches_per_step * args.steps,
-        "clocks": clock, "e2e": e2e, "cpu_baseline": cpu,
+        "config": {"workload": args.workload, "baseline_config": wl["config"], "M": wl["M"],
+                   "projections": [list(p) for p in proj], "bits": 4, "block_size": wl["bs"],
+                   "zero_points": "packed uint8" if wl["zp"] else "none",
+                   "l2": f"{head['layers']} rotating weight copies (> 3x L2)",
+                   "parallelism": f"column-shard x{world}" + (
+                       (" + peer-memory all-gather of Y" + (" overlapped within q/k/v and gate/up" if head["overlap"] else "")
+                        if head["peer"] else " + NCCL all-gather of Y") if world > 1 else ""),
+                   "cuda_graphs": head["graphs"], "paths": head["paths"]},
+        "roofline": head["roofline"], "kernels_us": head.get("kernels_us", {}),
+        "gpu_launches": head["launches"] * args.steps * (2 if world > 1 else 1),
+        "clocks": head["clocks"], "e2e": head.get("e2e"), "cpu_baseline": head.get("cpu_baseline"),
     }
+    if world > 1:
+        line["parity"] = head["parity"]
+    line.update(extra)
     print(json.dumps(line), flush=True)
 
 
@@ -480,11 +677,11 @@ def cpu_reference_time(wl, budget_s=15.0, kind_pref="reference", steps=None, war
     M = min(wl["M"], 16)
     lo, hi = wl["scale"]
     dt = np.float32 if wl.get("dtype") == "float32" else np.float16
+    act = 2 if dt == np.float16 else 4
     probs = []
     for (name, K, N) in wl["proj"]:
         kb = K // wl["bs"]
-        cols = max(threads * 4, 64)
-        cols = min(cols, N)
+        cols = min(max(threads * 4, 64), N)
         a = rng.standard_normal((M, K)).astype(dt)
         b = rng.integers(0, 256, (cols, kb, wl["bs"] // 2), dtype=np.uint8)
         s = rng.uniform(lo, hi, (cols, kb)).astype(dt)
@@ -505,7 +702,8 @@ def cpu_reference_time(wl, budget_s=15.0, kind_pref="reference", steps=None, war
     for _ in range(reps):
         one()
     dt_s = (time.perf_counter() - t) / reps
-    nbytes = sum(proj_bytes(M, K, cols, wl["bs"], wl["zp"], 2 if dt == np.float16 else 4) for (_, K, cols, *_r) in probs)
+    # bytes as read: the reference contract's float zero points ([N, kb] in A's dtype)
+    nbytes = sum(proj_bytes(M, K, cols, wl["bs"], wl["zp"], act, zp_bytes=act) for (_, K, cols, *_r) in probs)
     flops = sum(2 * M * K * cols for (_, K, cols, *_r) in probs)
     if wl["kind"] == "decode":
         value, unit = nbytes / dt_s / 1e9, "GB/s"
@@ -513,7 +711,7 @@ def cpu_reference_time(wl, budget_s=15.0, kind_pref="reference", steps=None, war
         value, unit = flops / dt_s / 1e12, "TFLOP/s"
     sample = (f"{len(probs)} projections x {probs[0][2]} output columns each, M={M}, full K; "
               f"{reps} timed repetitions of {dt_s * 1e3:.1f} ms")
-    return dict(value=round(value, 4), unit=unit, cores=threads, kind=kind, sample=sample,
+    return dict(value=round(value, 6), unit=unit, cores=threads, kind=kind, sample=sample,
                 impl="oracle/_ref (reference packedMatmul compiled as C++)" if kind == "reference" else "oracle/mmnb_oracle.c")
 
 
@@ -541,12 +739,14 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3_8b_decode")
     ap.add_argument("--layers", type=int, default=0, help="weight copies (default: > 3x L2)")
     ap.add_argument("--seed", type=int, default=2024)
-    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--no-overlap", action="store_true",
                     help="N > 1: run every all-gather on the compute stream (no overlap with independent GEMVs)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="omit the config-4 prefill object")
+    ap.add_argument("--no-strong", action="store_true", help="N > 1: omit the fixed-problem (strong) objects")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -554,7 +754,7 @@ def main():
     if args.impl == "reference":
         run_reference(args, wl)
     else:
-        run_ours(args, wl)
+        run_ours(args)
 
 
 if __name__ == "__main__":

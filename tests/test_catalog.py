@@ -6,9 +6,10 @@ from pathlib import Path
 
 import pytest
 
+from oracle.build import DEFAULT_REFERENCE  # XRGPU_REFERENCE_ROOT, the checkout the checkers use
 from xrgpu_b200 import catalog
 
-REFERENCE_CONTRACT = Path("/root/reference/kernels/com.microsoft.MatMulNBits/contract.json")
+REFERENCE_CONTRACT = DEFAULT_REFERENCE / "kernels/com.microsoft.MatMulNBits/contract.json"
 
 
 def test_catalog_loads():

@@ -149,13 +149,15 @@ def test_gemv_deterministic_and_linear_full_size(F):
 
 
 def test_gemv_caller_workspace_reused_across_calls(F):
-    """Shared tiles meet in the workspace and each call leaves its counters at zero: repeated calls
-    on one caller-owned workspace give identical results."""
+    """The GEMV needs no global scratch (its split-K partial sums meet in shared memory), so the
+    reported workspace size is 0; a caller-owned workspace argument is accepted and ignored, and
+    repeated calls give identical (deterministic) results within the tolerance of the oracle."""
     rng = np.random.default_rng(21)
     for (M, K, N, bs) in [(1, 4096, 4096, 32), (3, 14336, 1000, 64), (1, 576, 70, 32)]:
         a, b, s, zp, bias = make(rng, M, K, N, 4, bs, np.float16, "packed", bias=True)
         need = F.workspace_size(M, K=K, N=N, bits=4, block_size=bs)
-        ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
+        assert need == 0
+        ws = torch.zeros(64, dtype=torch.uint8, device="cuda")
         ys = [F.matmul_nbits(dev(a), dev(b), dev(s), dev(zp), dev(bias), K=K, N=N, block_size=bs, workspace=ws)
               for _ in range(3)]
         torch.cuda.synchronize()

@@ -199,3 +199,171 @@ def test_peer_allgather_two_gpus_matches_nccl():
     results = manager.dict()
     mp.start_processes(_peer_rank, args=(2, _free_port(), results), nprocs=2, start_method="spawn")
     assert all(results.get((r, i), False) for r in range(2) for i in range(4)), dict(results)
+
+
+# ----------------------------------------------------------------- shards of changing size on one group
+# (rows, shard columns) of float16 shards: 4 KB, 1 MB and 1 MB + 16 B (4 and 5 chunks per peer), prefill
+# shards of 7.3, 8 and 16 MB (28, 32 and 64 chunks), back to a decode shard, then the same again.
+ALTERNATING = [(1, 2048), (512, 1024), (1, 524296), (2048, 1792), (1, 2048), (4096, 1024), (1, 524296),
+               (1024, 8192), (512, 1024), (1, 4096)]
+
+
+def _alternating_rank(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    group = None
+    try:
+        from xrgpu_b200 import functional as F
+        from xrgpu_b200.p2p import PeerAllGather
+        group = PeerAllGather(max(r * c * 2 for r, c in ALTERNATING))
+        gen = torch.Generator(device="cuda")
+        ok = True
+        for rep in range(2):
+            for i, (M, S) in enumerate(ALTERNATING):
+                gen.manual_seed(1000 * rep + 10 * i + rank)
+                shard = torch.randn((M, S), generator=gen, device="cuda").to(torch.float16)
+                N = world * S - (8 if i % 3 == 1 else 0)  # a padded last shard on some calls
+                out = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+                group.all_gather(shard, out, N)
+                ref = torch.empty((world, M, S), dtype=torch.float16, device="cuda")
+                dist.all_gather_into_tensor(ref, shard)
+                ref = ref.permute(1, 0, 2).reshape(M, world * S)[:, :N]
+                ok &= torch.equal(out, ref)
+        torch.cuda.synchronize()
+        results[rank] = bool(ok) and F.device_error(rank) == 0
+    finally:
+        if group is not None:
+            group.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_peer_allgather_shards_of_changing_size_on_one_group():
+    """One group, successive calls whose shards fall in different chunk counts (the staging
+    parity must follow the call, not the chunk index): every call equals NCCL's all-gather."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_alternating_rank, args=(2, _free_port(), results), nprocs=2, start_method="spawn")
+    assert results.get(0) and results.get(1), dict(results)
+
+
+def test_epoch_slots_advance_once_per_call_for_any_chunk_count():
+    """Host model of the kernel's epoch bookkeeping: the CTA of chunk c advances slots
+    c, c + chunks, ... of its peer, so all 64 slots stay equal whatever the chunk counts."""
+    rng = np.random.default_rng(3)
+    slots = np.zeros(64, dtype=np.int64)
+    for call in range(1, 400):
+        chunks = int(rng.integers(4, 65))
+        e = {c: slots[c] + 1 for c in range(chunks)}  # every chunk CTA reads its own slot
+        assert len(set(e.values())) == 1 and e[0] == call
+        for c in range(chunks):
+            for s in range(c, 64, chunks):
+                slots[s] = e[c]
+        assert (slots == call).all()
+
+
+# ----------------------------------------------------------------- a peer that never arrives
+def _absent_peer(conn):
+    """Rank 1 of a two-rank group on the same GPU that exports its region and never calls."""
+    import ctypes
+    from xrgpu_b200 import _native
+    lib = _native.load()
+    handle = ctypes.create_string_buffer(_native.P2P_HANDLE_BYTES)
+    g = ctypes.c_void_p()
+    st = lib.xrgpu_p2p_create(0, 2, 1, 1 << 16, ctypes.byref(g), handle)
+    conn.send((st, handle.raw))
+    conn.recv()  # the other rank has finished
+    lib.xrgpu_p2p_destroy(g)
+    conn.close()
+
+
+@pytest.mark.gpu
+def test_peer_wait_gives_up_and_reports_0x401():
+    """A bounded device-side wait that runs out: rank 0's all-gather waits for a flag that rank 1
+    (another process, same GPU, never calling) does not set. The kernel gives up after 1 s,
+    records 0x401 in the device error word and returns; the context stays usable."""
+    import ctypes
+    from xrgpu_b200 import _native
+    from xrgpu_b200 import functional as F
+    lib = _native.load()
+    ctx = mp.get_context("spawn")
+    parent, child = ctx.Pipe()
+    proc = ctx.Process(target=_absent_peer, args=(child,))
+    proc.start()
+    g = ctypes.c_void_p()
+    try:
+        st, other = parent.recv()
+        assert st == 0
+        torch.cuda.set_device(0)
+        F.device_error(0, clear=True)
+        mine = ctypes.create_string_buffer(_native.P2P_HANDLE_BYTES)
+        _native.check(lib.xrgpu_p2p_create(0, 2, 0, 1 << 16, ctypes.byref(g), mine))
+        _native.check(lib.xrgpu_p2p_connect(g, mine.raw + other))
+        shard = torch.ones((1, 256), dtype=torch.float16, device="cuda")
+        out = torch.zeros((1, 512), dtype=torch.float16, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        _native.check(lib.xrgpu_p2p_allgather(g, ctypes.c_void_p(shard.data_ptr()), 1, 512,
+                                              ctypes.c_void_p(out.data_ptr()), 1024, 1024, ctypes.c_void_p(stream)))
+        torch.cuda.synchronize()
+        assert F.device_error(0, clear=True) == 0x401
+        assert torch.equal(out[:, :256], shard)          # this rank's own block was still written
+        assert torch.equal(out[:, 256:], torch.zeros_like(out[:, 256:]))  # the absent peer's was not
+        # the context is still usable: a GEMV runs and the word stays clear
+        a = torch.randn((1, 512), device="cuda").half()
+        b = torch.randint(0, 256, (64, 16, 16), dtype=torch.uint8, device="cuda")
+        s = torch.full((64, 16), 0.01, dtype=torch.float16, device="cuda")
+        F.matmul_nbits(a, b, s, K=512, N=64, block_size=32)
+        torch.cuda.synchronize()
+        assert F.device_error(0) == 0
+    finally:
+        if g.value:
+            torch.cuda.synchronize()
+            lib.xrgpu_p2p_destroy(g)
+        parent.send("done")
+        proc.join(timeout=60)
+    assert proc.exitcode == 0
+
+
+def _skipping_rank(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    group = None
+    try:
+        from xrgpu_b200 import _native
+        from xrgpu_b200 import functional as F
+        from xrgpu_b200.p2p import PeerAllGather
+        F.device_error(rank, clear=True)
+        group = PeerAllGather(1 << 16)
+        shard = torch.full((1, 1024), float(rank + 1), dtype=torch.float16, device="cuda")
+        out = torch.zeros((1, 2048), dtype=torch.float16, device="cuda")
+        group.all_gather(shard, out, 2048)  # both ranks: a normal call
+        group.check()
+        first_ok = torch.equal(out[:, 1024:], torch.full_like(out[:, 1024:], 2.0)) if rank == 0 else True
+        if rank == 0:  # rank 1 leaves out the second call, between steps
+            group.all_gather(shard, out, 2048)
+        try:
+            group.check()
+            raised = False
+        except _native.XrgpuError:
+            raised = True
+        results[rank] = (bool(first_ok), raised, group.broken)
+    finally:
+        if group is not None:
+            group.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_peer_wait_expires_when_a_rank_skips_a_call_two_gpus():
+    """On 2 GPUs rank 1 skips one all-gather: rank 0's kernel gives up after 1 s, records 0x401 and
+    returns; ``check()`` raises on rank 0 only and marks the group unusable."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_skipping_rank, args=(2, _free_port(), results), nprocs=2, start_method="spawn")
+    assert results.get(0) == (True, True, True) and results.get(1) == (True, False, False), dict(results)

@@ -7,19 +7,25 @@
 //   [0, 4 KB)       done flags: done[q][c] = last epoch in which rank q finished writing chunk c here
 //   [4 KB, ...)     staging[2][world][slot_bytes]: rank q's shard of epoch e lands in staging[e & 1][q]
 // The shard (rows x row bytes, contiguous) is cut into `chunks` byte chunks (4 for decode shards,
-// up to 64 of ~256 KB for large ones; every rank derives the same count from the same size). A
-// call on rank r (epoch e, counted per (peer, chunk)) runs one CTA per (peer p, chunk c):
+// up to 64 of ~256 KB for large ones; every rank derives the same count from the same size). Every
+// call advances ONE epoch per peer, whatever its chunk count: epoch[p][c] holds the same value for
+// all 64 chunk slots c of peer p, and the CTA of chunk c advances the slots c, c + chunks, c + 2 chunks,
+// ... so that each slot is advanced exactly once per call. A call on rank r (epoch e) runs one CTA per
+// (peer p, chunk c):
 //   * p == r: the CTA copies chunk c of r's own shard into r's block of Y;
 //   * p != r: the CTA stores chunk c of r's shard into p's staging[e & 1][r] (peer stores over
 //     NVLink), and after a CTA barrier one thread sets p's done[r][c] = e with a release store at
 //     system scope (the barrier orders every thread's stores before it, and release is cumulative);
 //     it then waits until its own done[p][c] >= e (acquire, bounded) and copies chunk c of p's shard
 //     from its own staging into p's block of Y.
-// Staging is double-buffered by epoch parity, so no "ready" handshake is needed: rank r writes
-// staging[e & 1][r] of p again only in epoch e + 2, after it has seen done[p] >= e + 1, which p
-// sets in its call e + 1 -- stream-ordered after p's call e has finished reading staging[e & 1].
+// Staging is double-buffered by epoch parity, so no "ready" handshake is needed. Rank r writes any
+// byte of p's staging[e & 1][r] in call e only after its call e - 1 completed, and that call saw
+// done[p][c] >= e - 1 for at least one chunk c. p sets that flag in its call e - 1, which starts
+// (griddepcontrol.wait, stream order) after p's call e - 2 -- the last reader of staging[e & 1] --
+// has finished. Because the epoch is per call, not per chunk, this holds whatever byte ranges the
+// chunks of calls e - 2 and e cover (shards of different sizes on one group).
 // Every rank must make the same sequence of calls on its group. Waits give up after 1 s and record
-// kErrPeerWait in the device error word (the results of that call are then undefined).
+// kErrPeerWait in the device error word; the group is then out of step and must be destroyed.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -38,7 +44,8 @@ struct xrgpu_p2p {
   char* local = nullptr;
   char* peers[XRGPU_P2P_MAX_WORLD] = {};
   bool opened[XRGPU_P2P_MAX_WORLD] = {};
-  uint32_t* epoch = nullptr;  // device [XRGPU_P2P_MAX_WORLD * 64]: epoch of the last call, per (peer, chunk)
+  uint32_t* epoch = nullptr;  // device [XRGPU_P2P_MAX_WORLD][64]: epoch of the last call per peer, one copy
+                              // per chunk slot (all 64 copies of a peer are equal between calls)
 };
 
 namespace xrgpu {
@@ -109,8 +116,8 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
   }
   __shared__ uint32_t epoch_s;
   __shared__ int ok_s;
-  uint32_t* epoch = q.epoch + p * kMaxChunks + c;
-  if (threadIdx.x == 0) epoch_s = *epoch + 1u;
+  uint32_t* epoch = q.epoch + p * kMaxChunks;  // kMaxChunks equal slots of peer p
+  if (threadIdx.x == 0) epoch_s = epoch[c] + 1u;
   __syncthreads();
   const uint32_t e = epoch_s;
   const int64_t slot_off = kFlagBytes + (static_cast<int64_t>(e & 1u) * q.world + q.rank) * q.slot_bytes;
@@ -138,7 +145,7 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
       }
     }
     ok_s = ok;
-    *epoch = e;
+    for (int slot = c; slot < kMaxChunks; slot += q.chunks) epoch[slot] = e;  // every slot once per call
   }
   __syncthreads();
   // 3. chunk c of p's shard from this rank's staging into p's block of Y

@@ -5,6 +5,10 @@ staging region, exchanges CUDA IPC handles over the ``torch.distributed`` group 
 ranks' regions; ``all_gather(shard, out)`` then enqueues one kernel on the current stream that
 leaves every rank's shard in ``out`` -- no NCCL call, so CUDA graphs capture it. Every rank must
 make the same sequence of calls. ``close()`` synchronises, waits for all ranks and unmaps.
+
+A peer that does not arrive within 1 s makes the kernel give up, record code 0x401 in the
+device's error word and return; every rank's epochs are then out of step, so the group cannot be
+used again. ``check()`` (after synchronising) reads and clears that word and raises.
 """
 from __future__ import annotations
 
@@ -34,6 +38,7 @@ class PeerAllGather:
         _native.check(lib.xrgpu_p2p_create(self.device.index, self.world, self.rank, self.slot_bytes,
                                            ctypes.byref(ptr), handle))
         self._g = ptr
+        self.broken = False
         handles = [None] * self.world
         dist.all_gather_object(handles, handle.raw, group=group)
         try:
@@ -50,6 +55,8 @@ class PeerAllGather:
         """
         if self._g is None:
             raise RuntimeError("peer all-gather group is closed")
+        if self.broken:
+            raise RuntimeError("peer all-gather group gave up waiting for a peer earlier; close it")
         if shard.dim() != 2 or not shard.is_contiguous() or out.dim() != 2 or out.stride(1) != 1:
             raise ValueError("shard must be a contiguous [M, S] tensor and out an [M, >= N] row-major view")
         es = shard.element_size()
@@ -58,6 +65,23 @@ class PeerAllGather:
             self._g, ctypes.c_void_p(shard.data_ptr()), shard.shape[0], shard.shape[1] * es,
             ctypes.c_void_p(out.data_ptr()), out.stride(0) * es, valid_cols * es, ctypes.c_void_p(stream)))
         return out
+
+    PEER_WAIT_EXPIRED = 0x401
+
+    def check(self) -> None:
+        """Synchronise this device, then raise ``XrgpuError`` if a call on it gave up waiting for a
+        peer (device error word 0x401, read and cleared). The group is marked unusable."""
+        if self._g is None:
+            return
+        torch.cuda.synchronize(self.device)
+        import ctypes as _ct
+        code = _ct.c_uint32(0)
+        _native.check(_native.load().xrgpu_device_error(self.device.index, _ct.byref(code), 1))
+        if code.value:
+            self.broken = True
+            raise _native.XrgpuError(_native.DEVICE_ERROR,
+                                     f"peer all-gather: device error 0x{code.value:x} (a peer did not arrive); "
+                                     "the group is out of step and must be closed")
 
     def close(self):
         """Unmap after every rank's last call: synchronise this device, host barrier, destroy."""

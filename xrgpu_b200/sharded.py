@@ -59,7 +59,8 @@ class ShardedMatMulNBits:
     def __init__(self, b: torch.Tensor, scales: torch.Tensor, zero_points: Optional[torch.Tensor] = None,
                  bias: Optional[torch.Tensor] = None, *, K: int, N: int, bits: int = 4, block_size: int,
                  group=None, compute: Optional[Callable] = None, peer_gather: Optional[bool] = None,
-                 peer_max_bytes: int = 64 << 20, peer_group=None, _presharded: bool = False):
+                 peer_max_bytes: int = 64 << 20, peer_group=None, peer_slot_bytes: int = 0,
+                 _presharded: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -83,6 +84,7 @@ class ShardedMatMulNBits:
         auto = (self.world > 1 and dist.is_initialized() and dist.get_backend(group) == "nccl" and same_node)
         self.peer_gather = auto if peer_gather is None else (bool(peer_gather) and self.world > 1)
         self.peer_max_bytes = int(peer_max_bytes)
+        self._peer_slot_bytes = int(peer_slot_bytes)  # minimum slot of this module's own group
         # A PeerAllGather shared with other modules (owned by the caller), or this module's own.
         self._shared_peer = peer_group
         self._peer = None
@@ -97,8 +99,13 @@ class ShardedMatMulNBits:
                    block_size=block_size, group=group, compute=compute, _presharded=True, **kw)
 
     def uses_peer_gather(self, M: int, element_size: int = 2) -> bool:
-        """Whether forward with M rows exchanges Y through peer memory (no NCCL call)."""
+        """Whether forward with M rows exchanges Y through peer memory (no NCCL call).
+
+        Mirrors the checks of ``xrgpu_p2p_allgather``: 16-byte shard rows (and output rows when
+        M > 1), a non-empty last shard (N > (world - 1) * S) and a shard within ``peer_max_bytes``.
+        """
         return (self.peer_gather and M * self.S * element_size <= self.peer_max_bytes
+                and self.N > (self.world - 1) * self.S
                 and (self.S * element_size) % 16 == 0 and (M == 1 or (self.N * element_size) % 16 == 0))
 
     def set_peer_group(self, peer_group) -> None:
@@ -112,10 +119,29 @@ class ShardedMatMulNBits:
                 raise ValueError(f"shared peer group slot ({self._shared_peer.slot_bytes} B) < shard ({nbytes} B)")
             return self._shared_peer
         if self._peer is None or self._peer.slot_bytes < nbytes:
+            # Creating (or growing) the group allocates device memory, synchronises and exchanges IPC
+            # handles over the process group: none of that can be recorded into a CUDA graph.
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(
+                    "ShardedMatMulNBits: the peer-memory group must exist before CUDA graph capture; run one "
+                    "forward with the largest M outside capture first, or pass peer_slot_bytes to the constructor")
             if self._peer is not None:
                 self._peer.close()
-            self._peer = PeerAllGather(max(nbytes, 1 << 16), group=self.group)
+            self._peer = PeerAllGather(max(nbytes, self._peer_slot_bytes, 1 << 16), group=self.group)
         return self._peer
+
+    def prepare_peer_group(self, max_rows: int, element_size: int = 2) -> None:
+        """Create this module's peer-memory group for up to ``max_rows`` rows now (collective), so
+        that later forwards -- including ones recorded into CUDA graphs -- allocate nothing."""
+        if self.world > 1 and self.uses_peer_gather(max_rows, element_size):
+            self._peer_group(max_rows * self.S * element_size)
+
+    def check_device_error(self) -> None:
+        """Raise if a peer-memory all-gather of this module gave up waiting for a peer (device code
+        0x401, after synchronising); the group is then out of step and is closed."""
+        for g in (self._shared_peer, self._peer):
+            if g is not None:
+                g.check()
 
     def close(self):
         """Release this module's own peer-memory group (collective: every rank calls it)."""
@@ -162,8 +188,10 @@ class ShardedMatMulNBits:
                 return out
             return y.reshape(*lead, self.N)
         if self.uses_peer_gather(M, y_local.element_size()):
-            dst = out.view(M, self.N) if out is not None else torch.empty((M, self.N), dtype=a.dtype, device=a.device)
-            group = self._peer_group(M * self.S * y_local.element_size())
+            es = y_local.element_size()
+            direct = out is not None and out.data_ptr() % 16 == 0 and (M == 1 or (out.view(M, self.N).stride(0) * es) % 16 == 0)
+            dst = out.view(M, self.N) if direct else torch.empty((M, self.N), dtype=a.dtype, device=a.device)
+            group = self._peer_group(M * self.S * es)
             if overlap:
                 ready = torch.cuda.Event()
                 ready.record()
@@ -174,6 +202,10 @@ class ShardedMatMulNBits:
                     self._gather_done.record()
             else:
                 group.all_gather(y_local, dst, self.N)
+            if out is not None and not direct:  # caller's buffer not 16-byte aligned: one copy
+                if overlap:
+                    self.wait_gather()
+                out.view(M, self.N).copy_(dst)
             return out if out is not None else dst.reshape(*lead, self.N)
         direct = out is not None and M == 1 and self.world * self.S == self.N and out.is_contiguous()
         gathered = (out.view(self.world, 1, self.S) if direct
