@@ -237,6 +237,179 @@ XRGPU_API int xrgpu_p2p_allgather(xrgpu_p2p* group, const void* shard, int64_t r
  * last all-gather on the group (synchronise, then a host barrier). */
 XRGPU_API int xrgpu_p2p_destroy(xrgpu_p2p* group);
 
+/* ---------------------------------------------------------------------------------------
+ * Operators around MatMulNBits: its fused callers and the operators that share its quantized
+ * formats. Same request model as above, with the reference's floating-point and string
+ * attributes and its requested-output list (xrgpu::operators::extended::Request and Attributes,
+ * runtime/include/xrgpu/extended_operators.h:8-28; attributes read by complex_plan.cpp:44-47).
+ *   com.microsoft.MatMulNBitsMlp (1027)  aT, skipT?, normScaleT?, gateBT, gateScalesT, gateBiasT?, upBT,
+ *                                         upScalesT, upBiasT?  -> yT, residualT?
+ *   com.microsoft.MatMulNBitsQkv (1028)  aT, skipT?, normScaleT, qBT, qScalesT, kBT, kScalesT, vBT, vScalesT
+ *                                         -> qT, kT, vT, residualT?
+ *   com.microsoft.MatMulBnb4 (1026)      aT, bT, absmaxT -> yT
+ *   com.microsoft.GatherBlockQuantized (1031)  dataT, indicesT, scalesT, zeroPointsT? -> outputT
+ *   com.microsoft.QMoE (1030)            inputT, routerT, fc1T, fc1ScalesT, fc2T, fc2ScalesT -> outputT
+ * (input lists: complex_plan.cpp:33-37,39-40; contracts: kernels/<operation>/contract.json).
+ * xrgpu_prepare / xrgpu_plan accept these operations too (integer attributes only);
+ * xrgpu_read_outputs / xrgpu_output_device_ptr take the output's index in the planned order.
+ * ------------------------------------------------------------------------------------- */
+typedef struct {
+  const char* name;
+  double value;
+} xrgpu_float_attr;
+
+typedef struct {
+  const char* name;
+  const char* value;
+} xrgpu_string_attr;
+
+/* extended::Request with every attribute kind (planner.cpp:72-85 precedence: args over attrs). */
+typedef struct {
+  const char* operation;
+  const xrgpu_tensor* inputs;
+  int32_t num_inputs;
+  const xrgpu_int_attr* attrs;
+  int32_t num_attrs;
+  const xrgpu_int_attr* args;
+  int32_t num_args;
+  const xrgpu_float_attr* float_attrs;
+  int32_t num_float_attrs;
+  const xrgpu_string_attr* string_attrs;
+  int32_t num_string_attrs;
+  const char* const* requested_outputs;  /* names in the wanted order; NULL/0 = the required outputs */
+  int32_t num_requested_outputs;
+} xrgpu_request_ex;
+
+/* extended::plan for every supported operation (complex_plan.cpp:58-143). */
+XRGPU_API int xrgpu_plan_ex(const xrgpu_request_ex* request, xrgpu_tensor* outputs, int32_t capacity, int32_t* count);
+
+/* Operator::prepare for every supported operation (extended_operators.h:51). */
+XRGPU_API int xrgpu_prepare_ex(const char* package_directory, const xrgpu_request_ex* request,
+                               const xrgpu_options* options, xrgpu_operator** out);
+
+/* Activation codes of the fused operators (complex_plan.cpp:50 activation_lower; fused,
+ * complex_kernel.glsl:41-47). */
+typedef enum {
+  XRGPU_ACT_NONE = 0,
+  XRGPU_ACT_RELU = 1,
+  XRGPU_ACT_SILU = 2,
+  XRGPU_ACT_GELU = 3,
+  XRGPU_ACT_TANH = 4,
+  XRGPU_ACT_SIGMOID = 5,
+  XRGPU_ACT_SWIGLU = 6
+} xrgpu_activation;
+
+/* MatMulNBitsMlp over device pointers (packedMatmul opcode 1027, complex_kernel.glsl:81,83):
+ *   h = a + skip; x = norm_scale ? h * (1/sqrt(sum(h^2)/K + epsilon) * norm_scale[k]) : h;
+ *   y = fused(x . dequant(gate)^T + gate_bias, activation) * (x . dequant(up)^T + up_bias);
+ *   residual (optional) = h. Weights use nbitWeight without zero points (z = 2^(bits-1)). */
+typedef struct {
+  int32_t dtype;           /* T1: XRGPU_FLOAT32 or XRGPU_FLOAT16 */
+  int32_t activation;      /* xrgpu_activation */
+  int64_t M, K, N, block_size, bits;
+  float epsilon;
+  int32_t reserved;
+  const void* a;           /* [M, K] */
+  const void* skip;        /* [M, K] or NULL */
+  const void* norm_scale;  /* [K] or NULL */
+  const uint8_t* gate_b;   /* [N, ceil(K/bs), ceil(bs*bits/8)] */
+  const void* gate_scales; /* [N, ceil(K/bs)] */
+  const void* gate_bias;   /* [N] or NULL */
+  const uint8_t* up_b;
+  const void* up_scales;
+  const void* up_bias;
+  void* y;                 /* [M, N] */
+  void* residual;          /* [M, K] or NULL */
+} xrgpu_mlp_problem;
+
+/* Device scratch bytes of xrgpu_mlp_forward (the normalised activations and the two projections). */
+XRGPU_API int xrgpu_mlp_workspace_size(const xrgpu_mlp_problem* p, uint64_t* bytes);
+/* workspace NULL: the library's per-device workspace (grown on demand). */
+XRGPU_API int xrgpu_mlp_forward(const xrgpu_mlp_problem* p, void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* MatMulNBitsQkv over device pointers (packedMatmul opcode 1028): x normalised as above (norm_scale
+ * required), q/k/v = x . dequant(W)^T (no zero points, no bias), residual (optional) = a + skip. */
+typedef struct {
+  int32_t dtype;
+  int32_t reserved;
+  int64_t M, K, Nq, Nkv, block_size, bits;
+  float epsilon;
+  int32_t reserved2;
+  const void* a;
+  const void* skip;
+  const void* norm_scale;
+  const uint8_t* q_b;
+  const void* q_scales;
+  const uint8_t* k_b;
+  const void* k_scales;
+  const uint8_t* v_b;
+  const void* v_scales;
+  void* q;                 /* [M, Nq] */
+  void* k;                 /* [M, Nkv] */
+  void* v;                 /* [M, Nkv] */
+  void* residual;          /* [M, K] or NULL */
+} xrgpu_qkv_problem;
+
+XRGPU_API int xrgpu_qkv_workspace_size(const xrgpu_qkv_problem* p, uint64_t* bytes);
+XRGPU_API int xrgpu_qkv_forward(const xrgpu_qkv_problem* p, void* workspace, uint64_t workspace_bytes, void* stream);
+
+/* MatMulBnb4 over device pointers (bnbWeight, complex_kernel.glsl:82; transB = 1):
+ * y[m, n] = sum_k a[m, k] * table[code(n*K + k)] * absmax[(n*K + k) / block_size], NF4 for
+ * quant_type 1, FP4 for 0, the high nibble of a byte first. */
+typedef struct {
+  int32_t dtype;
+  int32_t quant_type;
+  int64_t M, K, N, block_size;
+  const void* a;           /* [M, K] */
+  const uint8_t* b;        /* [ceil(N*K/2)] */
+  const void* absmax;      /* [ceil(N*K/block_size)] */
+  void* y;                 /* [M, N] */
+} xrgpu_bnb4_problem;
+
+XRGPU_API int xrgpu_bnb4_forward(const xrgpu_bnb4_problem* p, void* stream);
+
+/* GatherBlockQuantized over device pointers (gatherQuant, complex_kernel.glsl:85; gather_axis 0,
+ * quantize_axis 1): out[r, j] = (q - z) * scales[idx[r], j / block_size] as float32, zero points
+ * packed low-first (default 2^(bits-1)). An index outside [0, rows) leaves its row 0 and code 55
+ * in the device error word (the reference's fail(55)). */
+typedef struct {
+  int32_t bits;            /* 4 or 8 */
+  int32_t index_dtype;     /* XRGPU_INT64 or XRGPU_INT32 */
+  int64_t rows, row_bytes, count, block_size;
+  const uint8_t* data;     /* [rows, row_bytes] */
+  const void* indices;     /* [count] */
+  const float* scales;     /* [rows, ceil(width/block_size)], width = row_bytes * 8 / bits */
+  const uint8_t* zero_points; /* [rows, ceil(blocks*bits/8)] or NULL */
+  float* out;              /* [count, width] */
+} xrgpu_gather_problem;
+
+XRGPU_API int xrgpu_gather_block_quantized_forward(const xrgpu_gather_problem* p, void* stream);
+
+/* QMoE over device pointers (moe, complex_kernel.glsl:158-160), float32: the k experts of highest
+ * router score (ties: the higher expert index first) are weighted by a softmax over their scores;
+ * expert weights are symmetric (q - 2^(bits-1)) * scale with one scale per row (block_size 0) or
+ * per block of block_size columns; activation XRGPU_ACT_RELU, or XRGPU_ACT_SWIGLU with
+ * swiglu_fusion 1 (gate/linear rows interleaved), alpha/beta and an optional limit. */
+typedef struct {
+  int32_t bits;
+  int32_t activation;
+  int32_t swiglu_fusion;
+  int32_t has_swiglu_limit;
+  int64_t tokens, hidden, experts, k, fc1_rows, block_size;
+  float activation_alpha, activation_beta, swiglu_limit;
+  int32_t reserved;
+  const float* input;      /* [tokens, hidden] */
+  const float* router;     /* [tokens, experts] */
+  const uint8_t* fc1;      /* [experts, fc1_rows, ceil(hidden*bits/8)] */
+  const float* fc1_scales; /* [experts, fc1_rows] or [experts, fc1_rows, hidden/block_size] */
+  const uint8_t* fc2;      /* [experts, hidden, ceil(inter*bits/8)], inter = fc1_rows / (swiglu ? 2 : 1) */
+  const float* fc2_scales;
+  float* output;           /* [tokens, hidden] */
+} xrgpu_qmoe_problem;
+
+XRGPU_API int xrgpu_qmoe_workspace_size(const xrgpu_qmoe_problem* p, uint64_t* bytes);
+XRGPU_API int xrgpu_qmoe_forward(const xrgpu_qmoe_problem* p, void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* Library version string. */
 XRGPU_API const char* xrgpu_version(void);
 

@@ -25,7 +25,12 @@ EXPORTED = (
     "xrgpu_sync", "xrgpu_output_device_ptr", "xrgpu_mmnb_workspace_size", "xrgpu_mmnb_forward",
     "xrgpu_mmnb_dequantize", "xrgpu_mmnb_select_path", "xrgpu_device_error", "xrgpu_version",
     "xrgpu_p2p_create", "xrgpu_p2p_connect", "xrgpu_p2p_allgather", "xrgpu_p2p_destroy",
+    "xrgpu_plan_ex", "xrgpu_prepare_ex", "xrgpu_mlp_workspace_size", "xrgpu_mlp_forward", "xrgpu_qkv_workspace_size",
+    "xrgpu_qkv_forward", "xrgpu_bnb4_forward", "xrgpu_gather_block_quantized_forward", "xrgpu_qmoe_workspace_size",
+    "xrgpu_qmoe_forward",
 )
+# xrgpu_activation
+ACT_NONE, ACT_RELU, ACT_SILU, ACT_GELU, ACT_TANH, ACT_SIGMOID, ACT_SWIGLU = range(7)
 P2P_HANDLE_BYTES = 64
 P2P_MAX_WORLD = 16
 
@@ -56,6 +61,61 @@ class Problem_(ctypes.Structure):
                 ("block_size", ctypes.c_int64), ("bits", ctypes.c_int64), ("a", ctypes.c_void_p),
                 ("b", ctypes.c_void_p), ("scales", ctypes.c_void_p), ("zero_points", ctypes.c_void_p),
                 ("bias", ctypes.c_void_p), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64)]
+
+
+class FloatAttr_(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("value", ctypes.c_double)]
+
+
+class StringAttr_(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("value", ctypes.c_char_p)]
+
+
+class RequestEx_(ctypes.Structure):
+    _fields_ = [("operation", ctypes.c_char_p), ("inputs", ctypes.POINTER(Tensor_)), ("num_inputs", ctypes.c_int32),
+                ("attrs", ctypes.POINTER(IntAttr_)), ("num_attrs", ctypes.c_int32),
+                ("args", ctypes.POINTER(IntAttr_)), ("num_args", ctypes.c_int32),
+                ("float_attrs", ctypes.POINTER(FloatAttr_)), ("num_float_attrs", ctypes.c_int32),
+                ("string_attrs", ctypes.POINTER(StringAttr_)), ("num_string_attrs", ctypes.c_int32),
+                ("requested_outputs", ctypes.POINTER(ctypes.c_char_p)), ("num_requested_outputs", ctypes.c_int32)]
+
+
+_vp, _i64 = ctypes.c_void_p, ctypes.c_int64
+
+
+class MlpProblem_(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("activation", ctypes.c_int32), ("M", _i64), ("K", _i64), ("N", _i64),
+                ("block_size", _i64), ("bits", _i64), ("epsilon", ctypes.c_float), ("reserved", ctypes.c_int32),
+                ("a", _vp), ("skip", _vp), ("norm_scale", _vp), ("gate_b", _vp), ("gate_scales", _vp),
+                ("gate_bias", _vp), ("up_b", _vp), ("up_scales", _vp), ("up_bias", _vp), ("y", _vp), ("residual", _vp)]
+
+
+class QkvProblem_(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32), ("M", _i64), ("K", _i64), ("Nq", _i64),
+                ("Nkv", _i64), ("block_size", _i64), ("bits", _i64), ("epsilon", ctypes.c_float),
+                ("reserved2", ctypes.c_int32), ("a", _vp), ("skip", _vp), ("norm_scale", _vp), ("q_b", _vp),
+                ("q_scales", _vp), ("k_b", _vp), ("k_scales", _vp), ("v_b", _vp), ("v_scales", _vp), ("q", _vp),
+                ("k", _vp), ("v", _vp), ("residual", _vp)]
+
+
+class Bnb4Problem_(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int32), ("quant_type", ctypes.c_int32), ("M", _i64), ("K", _i64), ("N", _i64),
+                ("block_size", _i64), ("a", _vp), ("b", _vp), ("absmax", _vp), ("y", _vp)]
+
+
+class GatherProblem_(ctypes.Structure):
+    _fields_ = [("bits", ctypes.c_int32), ("index_dtype", ctypes.c_int32), ("rows", _i64), ("row_bytes", _i64),
+                ("count", _i64), ("block_size", _i64), ("data", _vp), ("indices", _vp), ("scales", _vp),
+                ("zero_points", _vp), ("out", _vp)]
+
+
+class QmoeProblem_(ctypes.Structure):
+    _fields_ = [("bits", ctypes.c_int32), ("activation", ctypes.c_int32), ("swiglu_fusion", ctypes.c_int32),
+                ("has_swiglu_limit", ctypes.c_int32), ("tokens", _i64), ("hidden", _i64), ("experts", _i64),
+                ("k", _i64), ("fc1_rows", _i64), ("block_size", _i64), ("activation_alpha", ctypes.c_float),
+                ("activation_beta", ctypes.c_float), ("swiglu_limit", ctypes.c_float), ("reserved", ctypes.c_int32),
+                ("input", _vp), ("router", _vp), ("fc1", _vp), ("fc1_scales", _vp), ("fc2", _vp),
+                ("fc2_scales", _vp), ("output", _vp)]
 
 
 _lib = None
@@ -98,6 +158,16 @@ def load(path: os.PathLike | None = None):
         "xrgpu_p2p_allgather": ([vp, vp, ctypes.c_int64, ctypes.c_int64, vp, ctypes.c_int64, ctypes.c_int64, vp],
                                 ctypes.c_int),
         "xrgpu_p2p_destroy": ([vp], ctypes.c_int),
+        "xrgpu_plan_ex": ([P(RequestEx_), P(Tensor_), i32, P(i32)], ctypes.c_int),
+        "xrgpu_prepare_ex": ([ctypes.c_char_p, P(RequestEx_), P(Options_), P(vp)], ctypes.c_int),
+        "xrgpu_mlp_workspace_size": ([P(MlpProblem_), P(u64)], ctypes.c_int),
+        "xrgpu_mlp_forward": ([P(MlpProblem_), vp, u64, vp], ctypes.c_int),
+        "xrgpu_qkv_workspace_size": ([P(QkvProblem_), P(u64)], ctypes.c_int),
+        "xrgpu_qkv_forward": ([P(QkvProblem_), vp, u64, vp], ctypes.c_int),
+        "xrgpu_bnb4_forward": ([P(Bnb4Problem_), vp], ctypes.c_int),
+        "xrgpu_gather_block_quantized_forward": ([P(GatherProblem_), vp], ctypes.c_int),
+        "xrgpu_qmoe_workspace_size": ([P(QmoeProblem_), P(u64)], ctypes.c_int),
+        "xrgpu_qmoe_forward": ([P(QmoeProblem_), vp, u64, vp], ctypes.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

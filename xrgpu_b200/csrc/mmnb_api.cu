@@ -29,6 +29,7 @@
 #include <thread>
 #include <vector>
 
+#include "mmnb_family_ops.h"
 #include "mmnb_internal.h"
 #include "xrgpu_mmnb.h"
 
@@ -231,6 +232,9 @@ int problem_from_c(const xrgpu_mmnb_problem* c, Problem* p, bool need_y) {
   return XRGPU_OK;
 }
 
+}  // namespace
+
+// ---------------------------------------------------------------- shared with the family operators
 int select_path(const Problem& p, int forced) {
   if (forced == kPathGeneric) return kPathGeneric;
   if (forced == kPathGemv) return gemv_supported(p) ? kPathGemv : -1;
@@ -325,8 +329,6 @@ std::string device_description(int dev) {
   return o.str();
 }
 
-}  // namespace
-
 int api_fail(int status, const std::string& message) { return fail(status, message); }
 
 int device_sm_count() {
@@ -361,6 +363,7 @@ struct xrgpu_operator {
   double execution_ms = 0, gpu_ms = -1;
   uint64_t dispatch_count = 0;
   std::string poison_reason;
+  xrgpu::FamilyOp* family = nullptr;  // the operations around MatMulNBits (mmnb_family_plan.cu)
 };
 
 namespace {
@@ -393,6 +396,7 @@ Problem operator_problem(const xrgpu_operator* op) {
 void release(xrgpu_operator* op) {
   DeviceGuard guard(op->device);
   if (op->stream) cudaStreamSynchronize(op->stream);
+  if (op->family) family_release(op->family);
   for (auto& ptr : op->dev_in) { if (ptr) cudaFree(ptr); ptr = nullptr; }
   if (op->dev_y) cudaFree(op->dev_y);
   op->dev_y = nullptr;
@@ -403,6 +407,32 @@ void release(xrgpu_operator* op) {
   op->ev_start = op->ev_stop = nullptr;
   if (op->stream) cudaStreamDestroy(op->stream);
   op->stream = nullptr;
+}
+
+// A request with integer attributes only, in the extended form.
+xrgpu_request_ex extend_request(const xrgpu_request* r) {
+  xrgpu_request_ex ex{};
+  ex.operation = r->operation;
+  ex.inputs = r->inputs;
+  ex.num_inputs = r->num_inputs;
+  ex.attrs = r->attrs;
+  ex.num_attrs = r->num_attrs;
+  ex.args = r->args;
+  ex.num_args = r->num_args;
+  return ex;
+}
+
+// The plain request of a MatMulNBits request given in the extended form (its attributes are integers).
+xrgpu_request plain_request(const xrgpu_request_ex* r) {
+  xrgpu_request p{};
+  p.operation = r->operation;
+  p.inputs = r->inputs;
+  p.num_inputs = r->num_inputs;
+  p.attrs = r->attrs;
+  p.num_attrs = r->num_attrs;
+  p.args = r->args;
+  p.num_args = r->num_args;
+  return p;
 }
 
 int check_open(const xrgpu_operator* op) {
@@ -473,6 +503,10 @@ int xrgpu_probe(char* json, uint64_t capacity, uint64_t* needed) {
 }
 
 int xrgpu_plan(const xrgpu_request* request, xrgpu_tensor* outputs, int32_t capacity, int32_t* count) {
+  if (request && is_family_operation(request->operation)) {
+    const xrgpu_request_ex ex = extend_request(request);
+    return xrgpu_plan_ex(&ex, outputs, capacity, count);
+  }
   Plan p;
   const int st = make_plan(request, false, &p);
   if (st) return st;
@@ -491,10 +525,14 @@ int xrgpu_plan(const xrgpu_request* request, xrgpu_tensor* outputs, int32_t capa
   return XRGPU_OK;
 }
 
-int xrgpu_prepare(const char* /*package_directory*/, const xrgpu_request* request, const xrgpu_options* options,
+int xrgpu_prepare(const char* package_directory, const xrgpu_request* request, const xrgpu_options* options,
                   xrgpu_operator** out) {
   if (!out) return fail(XRGPU_INVALID_ARGUMENT, "Null output handle");
   *out = nullptr;
+  if (request && is_family_operation(request->operation)) {
+    const xrgpu_request_ex ex = extend_request(request);
+    return xrgpu_prepare_ex(package_directory, &ex, options, out);
+  }
   Plan plan;
   int st = make_plan(request, true, &plan);
   if (st) return st;
@@ -563,6 +601,13 @@ int xrgpu_run_async(xrgpu_operator* op, void* stream) {
   if (st) return st;
   DeviceGuard guard(op->device);
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : op->stream;
+  if (op->family) {
+    st = family_launch(op->family, s);
+    if (st) return poison(op, st == XRGPU_INVALID_ARGUMENT ? XRGPU_RUNTIME_ERROR : st, xrgpu_last_error());
+    op->dispatch_count += 1;
+    op->executed = true;
+    return XRGPU_OK;
+  }
   const Problem p = operator_problem(op);
   const cudaError_t e = launch_path(p, op->path, op->workspace, s);
   if (e != cudaSuccess) return poison(op, XRGPU_RUNTIME_ERROR, std::string("kernel launch failed: ") + cudaGetErrorString(e));
@@ -602,11 +647,20 @@ int xrgpu_sync(xrgpu_operator* op) {
 int xrgpu_read_outputs(const xrgpu_operator* op, int32_t index, void* dst, uint64_t capacity) {
   int st = check_open(op);
   if (st) return st;
-  if (index != 0) return fail(XRGPU_INVALID_ARGUMENT, "MatMulNBits has one output (index 0, yT)");
-  if (capacity < op->y_bytes || (op->y_bytes && !dst)) return fail(XRGPU_INVALID_ARGUMENT, "output buffer too small");
+  void* src = op->dev_y;
+  uint64_t bytes = op->y_bytes;
+  if (op->family) {
+    if (index < 0 || index >= static_cast<int32_t>(op->family->out.size()))
+      return fail(XRGPU_INVALID_ARGUMENT, "output index outside the planned outputs");
+    src = op->family->out[index].dev;
+    bytes = op->family->out[index].nbytes;
+  } else if (index != 0) {
+    return fail(XRGPU_INVALID_ARGUMENT, "MatMulNBits has one output (index 0, yT)");
+  }
+  if (capacity < bytes || (bytes && !dst)) return fail(XRGPU_INVALID_ARGUMENT, "output buffer too small");
   DeviceGuard guard(op->device);
   if (!op->executed) return fail(XRGPU_RUNTIME_ERROR, "Operator has not run");
-  if (op->y_bytes && cudaMemcpyAsync(dst, op->dev_y, op->y_bytes, cudaMemcpyDeviceToHost, op->stream) != cudaSuccess)
+  if (bytes && cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, op->stream) != cudaSuccess)
     return fail(XRGPU_RUNTIME_ERROR, "device to host copy failed");
   if (cudaStreamSynchronize(op->stream) != cudaSuccess) return fail(XRGPU_RUNTIME_ERROR, "device to host copy failed");
   return XRGPU_OK;
@@ -615,7 +669,14 @@ int xrgpu_read_outputs(const xrgpu_operator* op, int32_t index, void* dst, uint6
 int xrgpu_output_device_ptr(const xrgpu_operator* op, int32_t index, void** ptr) {
   int st = check_open(op);
   if (st) return st;
-  if (index != 0 || !ptr) return fail(XRGPU_INVALID_ARGUMENT, "invalid output index or pointer");
+  if (!ptr) return fail(XRGPU_INVALID_ARGUMENT, "invalid output index or pointer");
+  if (op->family) {
+    if (index < 0 || index >= static_cast<int32_t>(op->family->out.size()))
+      return fail(XRGPU_INVALID_ARGUMENT, "invalid output index or pointer");
+    *ptr = op->family->out[index].dev;
+    return XRGPU_OK;
+  }
+  if (index != 0) return fail(XRGPU_INVALID_ARGUMENT, "invalid output index or pointer");
   *ptr = op->dev_y;
   return XRGPU_OK;
 }
@@ -624,6 +685,19 @@ int xrgpu_write_input(xrgpu_operator* op, const char* name, const void* data, ui
   int st = check_open(op);
   if (st) return st;
   if (!name) return fail(XRGPU_INVALID_ARGUMENT, "Null input name");
+  if (op->family) {
+    for (auto& t : op->family->in) {
+      if (t.name != name || !t.present) continue;
+      if (nbytes != t.nbytes || (nbytes && !data))
+        return fail(XRGPU_INVALID_ARGUMENT, std::string("Extended input byte count mismatch: ") + name);
+      DeviceGuard guard(op->device);
+      if (nbytes && cudaMemcpyAsync(t.dev, data, nbytes, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
+        return poison(op, XRGPU_RUNTIME_ERROR, "host to device copy failed");
+      if (cudaStreamSynchronize(op->stream) != cudaSuccess) return poison(op, XRGPU_RUNTIME_ERROR, "host to device copy failed");
+      return XRGPU_OK;
+    }
+    return fail(XRGPU_INVALID_ARGUMENT, std::string("Unknown prepared input: ") + name);
+  }
   int slot = -1;
   for (int s = 0; s < 5; ++s)
     if (std::strcmp(name, kInputNames[s]) == 0) slot = s;
@@ -639,6 +713,32 @@ int xrgpu_write_input(xrgpu_operator* op, const char* name, const void* data, ui
 int xrgpu_info(const xrgpu_operator* op, char* json, uint64_t capacity, uint64_t* needed) {
   if (!op) return fail(XRGPU_INVALID_ARGUMENT, "Null operator");
   std::ostringstream o;
+  if (op->family) {
+    const FamilyOp& f = *op->family;
+    o << "{\"backend\":\"cuda\",\"operation\":\"" << f.operation << "\",\"device\":\""
+      << json_escape(device_description(op->device)) << "\",\"cpu_compute_fallback\":false,\"execution_ms\":"
+      << op->execution_ms << ",\"gpu_ms\":";
+    if (op->gpu_ms >= 0) o << op->gpu_ms; else o << "null";
+    o << ",\"dispatch_count\":" << op->dispatch_count << ",\"executed\":" << (op->executed ? "true" : "false")
+      << ",\"closed\":" << (op->closed ? "true" : "false") << ",\"poisoned\":" << (op->poisoned ? "true" : "false")
+      << ",\"workspace_bytes\":" << f.workspace_bytes << ",\"inputs\":[";
+    bool first_in = true;
+    for (const auto& t : f.in) {
+      if (!t.present) continue;
+      o << (first_in ? "" : ",") << "{\"name\":\"" << t.name << "\",\"dtype\":\"" << dtype_name(t.dtype) << "\",\"shape\":[";
+      for (size_t i = 0; i < t.shape.size(); ++i) o << (i ? "," : "") << t.shape[i];
+      o << "]}";
+      first_in = false;
+    }
+    o << "],\"outputs\":[";
+    for (size_t j = 0; j < f.out.size(); ++j) {
+      o << (j ? "," : "") << "{\"name\":\"" << f.out[j].name << "\",\"dtype\":\"" << dtype_name(f.out[j].dtype) << "\",\"shape\":[";
+      for (size_t i = 0; i < f.out[j].shape.size(); ++i) o << (i ? "," : "") << f.out[j].shape[i];
+      o << "]}";
+    }
+    o << "]}";
+    return write_json(o.str(), json, capacity, needed);
+  }
   const Plan& p = op->plan;
   o << "{\"backend\":\"cuda\",\"operation\":\"" << kOperation << "\",\"device\":\"" << json_escape(device_description(op->device))
     << "\",\"cpu_compute_fallback\":false,\"path\":\"" << path_name(op->path) << "\",\"execution_ms\":" << op->execution_ms
@@ -673,7 +773,71 @@ int xrgpu_close(xrgpu_operator* op) {
 void xrgpu_destroy(xrgpu_operator* op) {
   if (!op) return;
   if (!op->closed) xrgpu_close(op);
+  delete op->family;
   delete op;
+}
+
+int xrgpu_plan_ex(const xrgpu_request_ex* request, xrgpu_tensor* outputs, int32_t capacity, int32_t* count) {
+  if (!request) return fail(XRGPU_INVALID_ARGUMENT, "Null request");
+  if (!is_family_operation(request->operation)) {
+    const xrgpu_request plain = plain_request(request);
+    return xrgpu_plan(&plain, outputs, capacity, count);
+  }
+  FamilyOp plan;
+  const int st = family_plan(request, false, &plan);
+  if (st) return st;
+  static const char* kNames[] = {"yT", "residualT", "qT", "kT", "vT", "outputT"};
+  if (count) *count = static_cast<int32_t>(plan.out.size());
+  for (int32_t i = 0; outputs && i < capacity && i < static_cast<int32_t>(plan.out.size()); ++i) {
+    xrgpu_tensor& y = outputs[i];
+    std::memset(&y, 0, sizeof(y));
+    for (const char* n : kNames)
+      if (plan.out[i].name == n) y.name = n;  // names with static storage
+    y.dtype = plan.out[i].dtype;
+    y.rank = static_cast<int32_t>(plan.out[i].shape.size());
+    for (size_t d = 0; d < plan.out[i].shape.size(); ++d) y.shape[d] = plan.out[i].shape[d];
+    y.nbytes = plan.out[i].nbytes;
+  }
+  return XRGPU_OK;
+}
+
+int xrgpu_prepare_ex(const char* package_directory, const xrgpu_request_ex* request, const xrgpu_options* options,
+                     xrgpu_operator** out) {
+  if (!out) return fail(XRGPU_INVALID_ARGUMENT, "Null output handle");
+  *out = nullptr;
+  if (!request) return fail(XRGPU_INVALID_ARGUMENT, "Null request");
+  if (!is_family_operation(request->operation)) {
+    const xrgpu_request plain = plain_request(request);
+    return xrgpu_prepare(package_directory, &plain, options, out);
+  }
+  FamilyOp plan;
+  int st = family_plan(request, true, &plan);
+  if (st) return st;
+  xrgpu_options opt;
+  xrgpu_default_options(&opt);
+  if (options) opt = *options;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) return fail(XRGPU_UNAVAILABLE, "no usable CUDA device");
+  if (opt.device < 0 || opt.device >= count) return fail(XRGPU_INVALID_ARGUMENT, "Invalid CUDA device ordinal");
+  auto* op = new xrgpu_operator();
+  op->options = opt;
+  op->device = opt.device;
+  op->family = new FamilyOp(std::move(plan));
+  DeviceGuard guard(op->device);
+  auto cleanup = [&](int status, const std::string& why) {
+    release(op);
+    delete op->family;
+    delete op;
+    return fail(status, why);
+  };
+  if (cudaStreamCreateWithFlags(&op->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return cleanup(XRGPU_RUNTIME_ERROR, "cudaStreamCreate failed");
+  if (cudaEventCreate(&op->ev_start) != cudaSuccess || cudaEventCreate(&op->ev_stop) != cudaSuccess)
+    return cleanup(XRGPU_RUNTIME_ERROR, "cudaEventCreate failed");
+  st = family_allocate(op->family, opt.memory_limit_bytes);
+  if (st) return cleanup(st, xrgpu_last_error());
+  *out = op;
+  return XRGPU_OK;
 }
 
 // ------------------------------------------------------------------ zero-copy API

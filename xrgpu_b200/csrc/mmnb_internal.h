@@ -63,4 +63,16 @@ int api_fail(int status, const std::string& message);
 unsigned* device_error_word();
 cudaError_t read_device_error(uint32_t* code, bool clear);
 
+// The planner's kernel choice for a problem (forced: a Path, kPathAuto = the planner's), -1 when a
+// forced path does not support it; its name; its scratch bytes; and its launch.
+int select_path(const Problem& p, int forced);
+const char* path_name(int path);
+uint64_t workspace_for(const Problem& p, int path);
+cudaError_t launch_path(const Problem& p, int path, void* ws, cudaStream_t s);
+// Per-device library workspace for callers that pass none (zero-filled, grows on demand).
+int library_workspace(uint64_t need, void** out);
+std::string json_escape(const std::string& s);
+int write_json(const std::string& s, char* out, uint64_t capacity, uint64_t* needed);
+std::string device_description(int dev);
+
 }  // namespace xrgpu

@@ -14,7 +14,11 @@ runtime/include/xrgpu/extended_operators.h:8-61):
   ``RuntimeError`` (``std::runtime_error``); a failed run poisons the operator
   until ``close()`` (kernels/_shared/extended/vulkan.cpp:105,115).
 
-Only ``com.microsoft.MatMulNBits`` is served by this backend.
+Operations served: ``com.microsoft.MatMulNBits`` and the operators around it --
+``com.microsoft.MatMulNBitsMlp``, ``MatMulNBitsQkv`` (its fused callers), ``MatMulBnb4``,
+``GatherBlockQuantized`` and ``QMoE`` (the same quantized-weight formats). Their attributes may be
+integers, numbers or strings, and optional outputs (``residualT``) are produced when requested,
+as in ``complex_plan.cpp:54-57``.
 """
 from __future__ import annotations
 
@@ -113,21 +117,44 @@ class Request:
     requested_outputs: List[Tensor] = field(default_factory=list)
 
 
-def _int_attrs(attrs: Attributes):
+def _int_attrs(attrs: Attributes, operation: str):
+    """Integer attributes; for MatMulNBits (integer attributes only) integral numbers count too."""
     items = []
     for k, v in attrs.integers.items():
         items.append((k, int(v)))
-    for k, v in attrs.numbers.items():
-        if float(v) != int(v):
-            raise ValueError(f"Integer attribute required: {k}")
-        items.append((k, int(v)))
-    if attrs.strings:
-        raise ValueError("Unknown string attribute for MatMulNBits: " + ", ".join(attrs.strings))
+    if operation == OPERATION:
+        for k, v in attrs.numbers.items():
+            if float(v) != int(v):
+                raise ValueError(f"Integer attribute required: {k}")
+            items.append((k, int(v)))
+        if attrs.strings:
+            raise ValueError("Unknown string attribute for MatMulNBits: " + ", ".join(attrs.strings))
     arr = (_native.IntAttr_ * max(1, len(items)))()
     for i, (k, v) in enumerate(items):
         arr[i].name = k.encode()
         arr[i].value = v
     return arr, len(items)
+
+
+def _other_attrs(attrs: Attributes, args: Attributes, operation: str, keep: list):
+    """Number and string attributes of the operators around MatMulNBits (args override attrs)."""
+    if operation == OPERATION:
+        return (_native.FloatAttr_ * 1)(), 0, (_native.StringAttr_ * 1)(), 0
+    numbers = {**attrs.numbers, **args.numbers}
+    strings = {**attrs.strings, **args.strings}
+    farr = (_native.FloatAttr_ * max(1, len(numbers)))()
+    for i, (k, v) in enumerate(numbers.items()):
+        name = k.encode()
+        keep.append(name)
+        farr[i].name = name
+        farr[i].value = float(v)
+    sarr = (_native.StringAttr_ * max(1, len(strings)))()
+    for i, (k, v) in enumerate(strings.items()):
+        name, value = k.encode(), str(v).encode()
+        keep += [name, value]
+        sarr[i].name = name
+        sarr[i].value = value
+    return farr, len(numbers), sarr, len(strings)
 
 
 class _CRequest:
@@ -143,7 +170,7 @@ class _CRequest:
             if t.layout != "contiguous":
                 raise ValueError("Extended kernels require contiguous row-major tensors")
             if t.storage_dtype not in (DType.Unspecified, t.dtype):
-                raise ValueError("CUDA MatMulNBits requires storage_dtype == dtype")
+                raise ValueError("the CUDA backend requires storage_dtype == dtype")
             ct = self.tensors[i]
             name = t.name.encode()
             self.keep.append(name)
@@ -158,9 +185,16 @@ class _CRequest:
                 self.keep.append(cbuf)
                 ct.data = ctypes.cast(cbuf, ctypes.c_void_p) if cbuf is not None else None
                 ct.nbytes = len(buf)
-        self.attrs, na = _int_attrs(request.attrs)
-        self.args, nr = _int_attrs(request.args)
-        self.req = _native.Request_(request.operation.encode(), self.tensors, n, self.attrs, na, self.args, nr)
+        self.attrs, na = _int_attrs(request.attrs, request.operation)
+        self.args, nr = _int_attrs(request.args, request.operation)
+        self.floats, nf, self.strings, ns = _other_attrs(request.attrs, request.args, request.operation, self.keep)
+        names = [t.name.encode() for t in request.requested_outputs]
+        self.keep += names
+        self.requested = (ctypes.c_char_p * max(1, len(names)))(*names)
+        op = request.operation.encode()
+        self.keep.append(op)
+        self.req = _native.RequestEx_(op, self.tensors, n, self.attrs, na, self.args, nr, self.floats, nf,
+                                      self.strings, ns, self.requested, len(names))
 
 
 def _check_requested(request: Request, planned: List[Tensor]):
@@ -179,11 +213,11 @@ def plan(request: Request) -> List[Tensor]:
     """Metadata-only validation and output inference (extended_operators.h:48)."""
     lib = _native.load()
     c = _CRequest(request, with_data=False)
-    out = (_native.Tensor_ * 1)()
+    out = (_native.Tensor_ * 8)()
     count = ctypes.c_int32(0)
-    check(lib.xrgpu_plan(ctypes.byref(c.req), out, 1, ctypes.byref(count)))
-    y = out[0]
-    planned = [Tensor(name=y.name.decode(), shape=[int(y.shape[i]) for i in range(y.rank)], dtype=DType(y.dtype))]
+    check(lib.xrgpu_plan_ex(ctypes.byref(c.req), out, 8, ctypes.byref(count)))
+    planned = [Tensor(name=y.name.decode(), shape=[int(y.shape[i]) for i in range(y.rank)], dtype=DType(y.dtype))
+               for y in out[:count.value]]
     _check_requested(request, planned)
     return planned
 
@@ -216,7 +250,7 @@ class Operator:
                                 int(options.device))
         handle = ctypes.c_void_p()
         pkg = package_directory.encode() if package_directory else None
-        check(lib.xrgpu_prepare(pkg, ctypes.byref(c.req), ctypes.byref(opts), ctypes.byref(handle)))
+        check(lib.xrgpu_prepare_ex(pkg, ctypes.byref(c.req), ctypes.byref(opts), ctypes.byref(handle)))
         return cls(handle, planned)
 
     def _handle(self):
