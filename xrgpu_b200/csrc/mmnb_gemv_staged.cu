@@ -132,14 +132,6 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint4 ldg_x128(const void* ptr) {
-  uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(ptr)
-               : "memory");
-  return v;
-}
 
 __device__ __forceinline__ float hsum2(uint32_t u) {
   const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u));
@@ -282,23 +274,32 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_staged_kernel(const _
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   for (int i = threadIdx.x; i < kZeroRegion / 16; i += kThreads) sts128(s_base + 16 * i, make_uint4(0u, 0u, 0u, 0u));
-  {
+  {  // Activations: up to eight 16-byte loads per thread are in flight before any is used, so staging
+     // costs one L2 round trip for K <= 8 * 8 * kThreads.
+    constexpr int kBatch = 8;
     const int groups16 = p.K / 8;
-    for (int base = 0; base < groups16; base += kThreads) {
-      const int idx = base + static_cast<int>(threadIdx.x);
-      const bool ok = idx < groups16;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (ok) v = ldg_x128(p.x + 8 * idx);
-      float sum = (hsum2(v.x) + hsum2(v.y)) + (hsum2(v.z) + hsum2(v.w));
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      if (ok) {
-        sts128(s_x + 16 * idx, make_uint4(prmt(v.x, v.z, 0x5410), prmt(v.y, v.w, 0x5410), prmt(v.x, v.z, 0x7632),
-                                          prmt(v.y, v.w, 0x7632)));
-        if ((idx & 3) == 0) {
-          const int chunk = idx >> 2, unit = chunk >> 2, cc = chunk & 3;  // unit = 4 win + jl
-          const uint32_t at = s_sums + 4u * (((unit >> 2) * 4 + cc) * 4 + (unit & 3));
-          asm volatile("st.shared.f32 [%0], %1;" ::"r"(at), "f"(sum * 5.9604644775390625e-8f) : "memory");
+    for (int base = 0; base < groups16; base += kThreads * kBatch) {
+      uint4 v[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int idx = base + j * kThreads + static_cast<int>(threadIdx.x);
+        v[j] = idx < groups16 ? __ldg(reinterpret_cast<const uint4*>(p.x) + idx) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        if (base + j * kThreads >= groups16) break;  // warp-uniform: groups16 is a multiple of 64
+        const int idx = base + j * kThreads + static_cast<int>(threadIdx.x);
+        float sum = (hsum2(v[j].x) + hsum2(v[j].y)) + (hsum2(v[j].z) + hsum2(v[j].w));
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (idx < groups16) {
+          sts128(s_x + 16 * idx, make_uint4(prmt(v[j].x, v[j].z, 0x5410), prmt(v[j].y, v[j].w, 0x5410),
+                                            prmt(v[j].x, v[j].z, 0x7632), prmt(v[j].y, v[j].w, 0x7632)));
+          if ((idx & 3) == 0) {
+            const int chunk = idx >> 2, unit = chunk >> 2, cc = chunk & 3;  // unit = 4 win + jl
+            const uint32_t at = s_sums + 4u * (((unit >> 2) * 4 + cc) * 4 + (unit & 3));
+            asm volatile("st.shared.f32 [%0], %1;" ::"r"(at), "f"(sum * 5.9604644775390625e-8f) : "memory");
+          }
         }
       }
     }
