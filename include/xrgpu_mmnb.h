@@ -327,6 +327,17 @@ XRGPU_API int xrgpu_mlp_workspace_size(const xrgpu_mlp_problem* p, uint64_t* byt
 /* workspace NULL: the library's per-device workspace (grown on demand). */
 XRGPU_API int xrgpu_mlp_forward(const xrgpu_mlp_problem* p, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* xrgpu_mlp_forward for callers that must not have the library allocate device memory (a serving
+ * engine that plans all GPU memory itself, a decode loop that cannot take cudaMalloc's implicit
+ * synchronisation). No counterpart in the reference, whose Operator owns every buffer it uses.
+ * The scratch is a fixed array of XRGPU_STATIC_SCRATCH_BYTES in device memory, held by every GPU that
+ * loads the library until the process exits; problems whose xrgpu_mlp_workspace_size is larger are
+ * rejected with XRGPU_INVALID_ARGUMENT. The caller still passes inputs and outputs. The first call on
+ * a device looks up the array's device address (make that call before any stream capture). All calls
+ * share the array: calls that overlap on the GPU race. Calls no allocator. */
+#define XRGPU_STATIC_SCRATCH_BYTES (4u << 20)
+XRGPU_API int xrgpu_mlp_forward_static(const xrgpu_mlp_problem* p, void* stream);
+
 /* MatMulNBitsQkv over device pointers (packedMatmul opcode 1028): x normalised as above (norm_scale
  * required), q/k/v = x . dequant(W)^T (no zero points, no bias), residual (optional) = a + skip. */
 typedef struct {

@@ -25,7 +25,8 @@ EXPORTED = (
     "xrgpu_sync", "xrgpu_output_device_ptr", "xrgpu_mmnb_workspace_size", "xrgpu_mmnb_forward",
     "xrgpu_mmnb_dequantize", "xrgpu_mmnb_select_path", "xrgpu_device_error", "xrgpu_version",
     "xrgpu_p2p_create", "xrgpu_p2p_connect", "xrgpu_p2p_allgather", "xrgpu_p2p_destroy",
-    "xrgpu_plan_ex", "xrgpu_prepare_ex", "xrgpu_mlp_workspace_size", "xrgpu_mlp_forward", "xrgpu_qkv_workspace_size",
+    "xrgpu_plan_ex", "xrgpu_prepare_ex", "xrgpu_mlp_workspace_size", "xrgpu_mlp_forward", "xrgpu_mlp_forward_static",
+    "xrgpu_qkv_workspace_size",
     "xrgpu_qkv_forward", "xrgpu_bnb4_forward", "xrgpu_gather_block_quantized_forward", "xrgpu_qmoe_workspace_size",
     "xrgpu_qmoe_forward",
 )
@@ -33,6 +34,7 @@ EXPORTED = (
 ACT_NONE, ACT_RELU, ACT_SILU, ACT_GELU, ACT_TANH, ACT_SIGMOID, ACT_SWIGLU = range(7)
 P2P_HANDLE_BYTES = 64
 P2P_MAX_WORLD = 16
+STATIC_SCRATCH_BYTES = 4 << 20  # XRGPU_STATIC_SCRATCH_BYTES (xrgpu_mlp_forward_static)
 
 
 class Tensor_(ctypes.Structure):
@@ -162,6 +164,7 @@ def load(path: os.PathLike | None = None):
         "xrgpu_prepare_ex": ([ctypes.c_char_p, P(RequestEx_), P(Options_), P(vp)], ctypes.c_int),
         "xrgpu_mlp_workspace_size": ([P(MlpProblem_), P(u64)], ctypes.c_int),
         "xrgpu_mlp_forward": ([P(MlpProblem_), vp, u64, vp], ctypes.c_int),
+        "xrgpu_mlp_forward_static": ([P(MlpProblem_), vp], ctypes.c_int),
         "xrgpu_qkv_workspace_size": ([P(QkvProblem_), P(u64)], ctypes.c_int),
         "xrgpu_qkv_forward": ([P(QkvProblem_), vp, u64, vp], ctypes.c_int),
         "xrgpu_bnb4_forward": ([P(Bnb4Problem_), vp], ctypes.c_int),
