@@ -185,8 +185,9 @@ typedef struct {
   int64_t ldy;              /* row stride of y in elements; 0 means N */
 } xrgpu_mmnb_problem;
 
-/* Device scratch bytes xrgpu_mmnb_forward needs for this problem (split-K partial sums and
- * tile counters; may be 0). */
+/* Device scratch bytes xrgpu_mmnb_forward needs for this problem. Every kernel path of this
+ * build reports 0: the GEMV's K slices meet in shared memory and the GEMM keeps whole K per tile.
+ * The argument stays so that a path which needs global scratch can be added without an ABI change. */
 XRGPU_API int xrgpu_mmnb_workspace_size(const xrgpu_mmnb_problem* p, uint64_t* bytes);
 
 /* Enqueues Y = A.dequant(B)^T (+bias) on `stream` (cudaStream_t, NULL = legacy default).
@@ -204,8 +205,12 @@ XRGPU_API int xrgpu_mmnb_dequantize(const xrgpu_mmnb_problem* p, float* w, void*
 /* Name of the kernel path the planner selects for p ("generic", "gemv", "gemm"). */
 XRGPU_API int xrgpu_mmnb_select_path(const xrgpu_mmnb_problem* p, char* name, uint64_t capacity);
 
-/* Reads (and optionally clears) the device error word of `device`: 0 = no error; otherwise a
- * code (1 = bounded wait expired in a kernel). */
+/* Reads (and optionally clears) the device error word of `device`: 0 = no error; otherwise the
+ * code of the first bounded wait that expired in a kernel (each wait gives up after about 1 s):
+ *   0x301..0x305  prefill GEMM: producer, MMA, dequantisation, epilogue wait, final drain;
+ *   0x401         peer all-gather: a peer's flag did not arrive. The group's epochs have then
+ *                 advanced past the failed call, so the group must be destroyed, not reused.
+ * The kernel that gave up returns normally and leaves the context usable; its output is undefined. */
 XRGPU_API int xrgpu_device_error(int32_t device, uint32_t* code, int32_t clear);
 
 /* ---- Peer-memory all-gather for column-sharded MatMulNBits (no counterpart in the reference,

@@ -6,6 +6,8 @@
 // Each rank owns one region (cudaMalloc, shared with the other ranks by CUDA IPC):
 //   [0, 4 KB)       done flags: done[q][c] = last epoch in which rank q finished writing chunk c here
 //   [4 KB, ...)     staging[2][world][slot_bytes]: rank q's shard of epoch e lands in staging[e & 1][q]
+//   then            words[2][world][ll_bytes]: the same for the low-latency form below (kept apart, so
+//                   that raw shard bytes are never read as words)
 // The shard (rows x row bytes, contiguous) is cut into `chunks` byte chunks (4 for decode shards,
 // up to 64 of ~256 KB for large ones; every rank derives the same count from the same size). Every
 // call advances ONE epoch per peer, whatever its chunk count: epoch[p][c] holds the same value for
@@ -24,6 +26,12 @@
 // (griddepcontrol.wait, stream order) after p's call e - 2 -- the last reader of staging[e & 1] --
 // has finished. Because the epoch is per call, not per chunk, this holds whatever byte ranges the
 // chunks of calls e - 2 and e cover (shards of different sizes on one group).
+// Shards up to kLLMaxBytes (decode) take a lower-latency form of the same exchange: every 8-byte
+// word sent carries 4 bytes of the shard and the call's epoch, written with one 64-bit store (single-
+// copy atomic), so the receiver polls the words themselves until each holds epoch e and no fence,
+// release or separate flag is needed on either side. Such a shard takes twice its size in staging;
+// the same parity and per-call epoch argument covers it (a word of an older call holds an older
+// epoch and is not taken).
 // Every rank must make the same sequence of calls on its group. Waits give up after 1 s and record
 // kErrPeerWait in the device error word; the group is then out of step and must be destroyed.
 #include <cuda_runtime.h>
@@ -40,7 +48,9 @@
 
 struct xrgpu_p2p {
   int device = 0, world = 0, rank = 0;
-  uint64_t slot_bytes = 0, region_bytes = 0;
+  uint64_t slot_bytes = 0;   // largest shard a call may pass (raw staging per parity and rank)
+  uint64_t ll_bytes = 0;     // word staging per parity and rank: 2 x min(slot_bytes, kLLMaxBytes)
+  uint64_t region_bytes = 0;
   char* local = nullptr;
   char* peers[XRGPU_P2P_MAX_WORLD] = {};
   bool opened[XRGPU_P2P_MAX_WORLD] = {};
@@ -53,7 +63,14 @@ namespace {
 
 constexpr int kMaxChunks = 64;                              // CTAs per peer at most
 constexpr int kFlagBytes = XRGPU_P2P_MAX_WORLD * kMaxChunks * 4;  // one done flag per (rank, chunk)
-constexpr int kThreads = 256;  // small enough to sit beside a running GEMV CTA
+// Threads per CTA: 256 for large shards (copy bandwidth), 128 for decode-sized ones, so that a CTA
+// (40 registers a thread: 5,120 a CTA) fits in the 8,192 registers a decode GEMV CTA leaves free on
+// its SM and a spinning all-gather never holds an SM that the next GEMV's CTA is waiting for.
+constexpr int kThreads = 256;
+constexpr int kSmallThreads = 128;
+constexpr int64_t kSmallShardBytes = 1 << 20;
+constexpr int64_t kLLMaxBytes = 1 << 20;  // shards up to 1 MB travel as (4 data bytes, epoch) words
+constexpr int64_t kLLPairsPerThread = 4;  // 16-byte word pairs a thread sends per chunk at most
 constexpr int kMinChunks = 4;  // CTAs per peer for small shards: the peer stores spread over 4 SMs
 constexpr int64_t kChunkBytes = 256 * 1024;  // target chunk size for large shards
 constexpr unsigned kErrPeerWait = 0x401;
@@ -63,10 +80,19 @@ struct P2PParams {
   uint32_t* epoch;
   const char* shard;  // [rows][srb]
   char* out;          // [rows][orb], rank q's block at byte q * srb, first ovb bytes of a row valid
-  int64_t rows, srb, orb, ovb, slot_bytes;
+  int64_t rows, srb, orb, ovb, slot_bytes, ll_bytes;
   int world, rank, chunks;
   unsigned* err;
 };
+
+// One 16-byte vector of two 64-bit elements: each element is written and read as one single-copy
+// atomic access, so a word's data and epoch are always seen together.
+__device__ __forceinline__ void st_ll_pair(void* p, uint64_t w0, uint64_t w1) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(w0), "l"(w1) : "memory");
+}
+__device__ __forceinline__ void ld_ll_pair(const void* p, uint64_t& w0, uint64_t& w1) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p) : "memory");
+}
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -155,6 +181,76 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_kernel(const __grid_co
   }
 }
 
+// Low-latency form (shards of at most kLLMaxBytes). CTA (p, c) handles 8-byte pair range
+// [lo, hi) of the shard. p == rank: copies it into Y. p != rank: sends it to p as words
+// (data | e << 32) into p's staging[e & 1][rank] (16 bytes per 8 data bytes), then polls its own
+// staging[e & 1][p] until both words of each of its pairs hold epoch e and writes their data into
+// p's block of Y. No fence is needed: a word carries its own validity.
+__global__ void __launch_bounds__(kThreads) p2p_allgather_ll_kernel(const __grid_constant__ P2PParams q) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int p = static_cast<int>(blockIdx.x) / q.chunks, c = static_cast<int>(blockIdx.x) % q.chunks;
+  const int64_t pairs = q.rows * q.srb / 8;
+  const int64_t per = (pairs + q.chunks - 1) / q.chunks;
+  const int64_t lo = per * c < pairs ? per * c : pairs, hi = per * (c + 1) < pairs ? per * (c + 1) : pairs;
+  const int64_t block_off = static_cast<int64_t>(p) * q.srb;
+  const int64_t valid = q.ovb - block_off;
+  if (p == q.rank) {  // copy_chunk wants 16-byte bounds: split the bytes in 16-byte units instead
+    const int64_t bytes = q.rows * q.srb, per16 = (bytes / 16 + q.chunks - 1) / q.chunks * 16;
+    const int64_t blo = per16 * c < bytes ? per16 * c : bytes, bhi = per16 * (c + 1) < bytes ? per16 * (c + 1) : bytes;
+    copy_chunk<false>(q.out + block_off, q.orb, q.shard, q.srb, blo, bhi, valid);
+    return;
+  }
+  __shared__ uint32_t epoch_s;
+  uint32_t* epoch = q.epoch + p * kMaxChunks;
+  if (threadIdx.x == 0) epoch_s = epoch[c] + 1u;
+  __syncthreads();
+  const uint32_t e = epoch_s;
+  const uint64_t tag = static_cast<uint64_t>(e) << 32;
+  const int64_t ll_base = kFlagBytes + 2 * static_cast<int64_t>(q.world) * q.slot_bytes;
+  const int64_t par_off = ll_base + static_cast<int64_t>(e & 1u) * q.world * q.ll_bytes;
+  // 1. send: 8 data bytes -> one 16-byte pair of words
+  {
+    char* dst = q.peers[p] + par_off + static_cast<int64_t>(q.rank) * q.ll_bytes;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+      const uint2 d = *reinterpret_cast<const uint2*>(q.shard + 8 * i);
+      st_ll_pair(dst + 16 * i, tag | d.x, tag | d.y);
+    }
+  }
+  // 2. receive p's pairs of this range from this rank's staging
+  const char* src = q.peers[q.rank] + par_off + static_cast<int64_t>(p) * q.ll_bytes;
+  const int64_t width = valid < q.srb ? valid : q.srb;
+  bool ok = true;
+  for (int64_t i = lo + threadIdx.x; i < hi && ok; i += blockDim.x) {
+    uint64_t w0, w1;
+    ld_ll_pair(src + 16 * i, w0, w1);
+    if (static_cast<uint32_t>(w0 >> 32) != e || static_cast<uint32_t>(w1 >> 32) != e) {
+      const uint64_t start = global_timer_ns();
+      do {
+        if (global_timer_ns() - start > kWaitLimitNs) {
+          record_device_error(q.err, kErrPeerWait);
+          ok = false;
+          break;
+        }
+        ld_ll_pair(src + 16 * i, w0, w1);
+      } while (static_cast<uint32_t>(w0 >> 32) != e || static_cast<uint32_t>(w1 >> 32) != e);
+      if (!ok) break;
+    }
+    const int64_t m = (8 * i) / q.srb, j = 8 * i - m * q.srb;
+    if (j >= width) continue;
+    char* o = q.out + block_off + m * q.orb + j;
+    const uint32_t d0 = static_cast<uint32_t>(w0), d1 = static_cast<uint32_t>(w1);
+    if (j + 8 <= width) {
+      *reinterpret_cast<uint2*>(o) = make_uint2(d0, d1);
+    } else {  // ragged end of the last block
+      for (int64_t t = 0; t < width - j; ++t) o[t] = static_cast<char>((t < 4 ? d0 >> (8 * t) : d1 >> (8 * (t - 4))) & 0xff);
+    }
+  }
+  __syncthreads();  // every thread has read epoch_s
+  if (threadIdx.x == 0)
+    for (int slot = c; slot < kMaxChunks; slot += q.chunks) epoch[slot] = e;  // every slot once per call
+}
+
 }  // namespace
 }  // namespace xrgpu
 
@@ -180,7 +276,8 @@ int xrgpu_p2p_create(int32_t device, int32_t world, int32_t rank, uint64_t slot_
     g->world = world;
     g->rank = rank;
     g->slot_bytes = align_up(slot_bytes, 256);
-    g->region_bytes = kFlagBytes + 2 * static_cast<uint64_t>(world) * g->slot_bytes;
+    g->ll_bytes = 2 * std::min<uint64_t>(g->slot_bytes, kLLMaxBytes);
+    g->region_bytes = kFlagBytes + 2 * static_cast<uint64_t>(world) * (g->slot_bytes + g->ll_bytes);
     cudaIpcMemHandle_t h;
     if (cudaMalloc(&g->local, g->region_bytes) != cudaSuccess || cudaMemset(g->local, 0, g->region_bytes) != cudaSuccess ||
         cudaMalloc(&g->epoch, sizeof(uint32_t) * XRGPU_P2P_MAX_WORLD * kMaxChunks) != cudaSuccess ||
@@ -252,24 +349,31 @@ int xrgpu_p2p_allgather(xrgpu_p2p* g, const void* shard, int64_t rows, int64_t s
   q.orb = out_row_bytes;
   q.ovb = out_valid_bytes;
   q.slot_bytes = static_cast<int64_t>(g->slot_bytes);
+  q.ll_bytes = static_cast<int64_t>(g->ll_bytes);
   q.world = g->world;
   q.rank = g->rank;
   const int64_t bytes = rows * shard_row_bytes;
-  q.chunks = static_cast<int>(std::min<int64_t>(kMaxChunks, std::max<int64_t>(kMinChunks, (bytes + kChunkBytes - 1) / kChunkBytes)));
+  const bool ll = bytes <= kLLMaxBytes;
+  if (ll) {  // enough CTAs per peer that a thread sends at most kLLPairsPerThread pairs
+    const int64_t per_cta = kSmallThreads * kLLPairsPerThread;
+    q.chunks = static_cast<int>(std::min<int64_t>(kMaxChunks, std::max<int64_t>(1, (bytes / 8 + per_cta - 1) / per_cta)));
+  } else {
+    q.chunks = static_cast<int>(std::min<int64_t>(kMaxChunks, std::max<int64_t>(kMinChunks, (bytes + kChunkBytes - 1) / kChunkBytes)));
+  }
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(g->device);
   q.err = device_error_word();
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(g->world * q.chunks), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(bytes <= kSmallShardBytes ? kSmallThreads : kThreads, 1, 1);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, p2p_allgather_kernel, q);
+  const cudaError_t e = ll ? cudaLaunchKernelEx(&cfg, p2p_allgather_ll_kernel, q) : cudaLaunchKernelEx(&cfg, p2p_allgather_kernel, q);
   cudaSetDevice(prev);
   if (e != cudaSuccess) return api_fail(XRGPU_RUNTIME_ERROR, std::string("peer all-gather launch failed: ") + cudaGetErrorString(e));
   return XRGPU_OK;
