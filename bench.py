@@ -270,7 +270,7 @@ class Runner:
         self.ys = {n: torch.empty((self.M, N), device=dev, dtype=self.dt) for (n, K, N) in self.full_proj}
         self.weights, self.full = [], []
         self.keep_full = min(self.layers, 4) if (self.mode == "strong" and self.world > 1) else 0
-        shared_bytes = 0
+        shard_bytes = {}
         for layer in range(self.layers):
             projs = []
             for (name, K, N) in wl["proj"]:
@@ -287,7 +287,7 @@ class Runner:
                         mod = ShardedMatMulNBits.from_shard(p["b"], p["s"], p["zp"], None, K=K, N=Nf, block_size=wl["bs"])
                     else:
                         mod = ShardedMatMulNBits(p["b"], p["s"], p["zp"], None, K=K, N=Nf, block_size=wl["bs"])
-                    shared_bytes = max(shared_bytes, self.M * mod.S * self.act_bytes)
+                    shard_bytes[name] = self.M * mod.S * self.act_bytes
                     mods.append(dict(name=name, K=K, N=Nf, mod=mod))
                 if layer < self.keep_full:
                     self.full.append(projs)  # full weights of this layer, for the single-GPU comparison
@@ -299,14 +299,21 @@ class Runner:
                                            for layer in self.weights for p in layer)
         if self.peer:
             from xrgpu_b200.p2p import PeerAllGather
-            # one peer-memory group shared by every projection (calls are stream-ordered), created
-            # before any capture
-            self.shared = PeerAllGather(shared_bytes)
+            # one peer-memory group per projection, shared by its copies in every layer and created
+            # before any capture: a projection's calls alternate send and receive on its own group,
+            # so the gathers of different projections may be in flight together
+            self.shared = {name: PeerAllGather(nbytes) for name, nbytes in shard_bytes.items()}
             for layer in self.weights:
                 for p in layer:
-                    p["mod"].set_peer_group(self.shared)
-        self.overlap = self.peer and not self.args.no_overlap
-        self.comm = torch.cuda.Stream(dev) if self.overlap else None
+                    p["mod"].set_peer_group(self.shared[p["name"]])
+        # How the peer-memory exchanges of a step are ordered (N > 1): "defer" enqueues each exchange
+        # on the compute stream just before the first kernel that needs its Y (one stream, every
+        # launch early behind the previous one); "stream" runs them on a side stream joined by events;
+        # "inline" puts each right after its own GEMV.
+        mode = "inline" if self.args.no_overlap else self.args.gather_mode
+        self.gather_mode = mode if self.peer else "inline"
+        self.overlap = self.gather_mode != "inline"
+        self.comm = torch.cuda.Stream(dev) if self.gather_mode == "stream" else None
         self.graphs = []
 
     def _path(self, K, N):
@@ -329,13 +336,15 @@ class Runner:
                 x = self.acts[p["K"]]
                 if self.world == 1:
                     self.F.matmul_nbits(x, p["b"], p["s"], p["zp"], K=p["K"], N=p["N"], block_size=bs, out=self.ys[name])
-                elif self.overlap:  # the gather runs beside the group's other kernels
+                elif self.gather_mode == "stream":  # the gather runs beside the group's other kernels
                     p["mod"](x, out=self.ys[name], gather_stream=self.comm)
+                elif self.gather_mode == "defer":  # the gather waits on this stream until the group ends
+                    p["mod"](x, out=self.ys[name], defer=True)
                 else:
                     p["mod"](x, out=self.ys[name])
             if self.world > 1 and self.overlap:
-                for name in grp:
-                    projs[name]["mod"].wait_gather()
+                from xrgpu_b200.sharded import ShardedMatMulNBits
+                ShardedMatMulNBits.wait_gather_all([projs[name]["mod"] for name in grp])
 
     def step_full(self, layer):
         """The unsharded problem of a kept layer on this GPU alone (strong-scaling comparison)."""
@@ -530,8 +539,8 @@ class Runner:
             for layer in self.weights:
                 for p in layer:
                     p["mod"].close()
-            if self.shared is not None:
-                self.shared.close()  # collective: every rank closes it at the same point
+            for name in sorted(self.shared or {}):
+                self.shared[name].close()  # collective: every rank closes them in the same order
 
 
 def roofline_of(runner, step_ms, pk, pk_kind):
@@ -583,7 +592,7 @@ def measure(name, args, world, rank, local, device, *, mode="weak", headline=Fal
                unit="GB/s" if wl["kind"] == "decode" else "TFLOP/s",
                metric="MatMulNBits decode GB/s" if wl["kind"] == "decode" else "MatMulNBits prefill TFLOP/s",
                roofline=roofline_of(runner, step_ms, pk, pk_kind), graphs=runner.graphable,
-               overlap=runner.overlap, peer=runner.peer, launches=len(wl["proj"]))
+               overlap=runner.overlap, gather_mode=runner.gather_mode, peer=runner.peer, launches=len(wl["proj"]))
     attach_traffic(res["roofline"], name)
     if world == 1:
         res["kernels_us"] = runner.kernel_times()
@@ -649,7 +658,8 @@ def run_ours(args):
                    "zero_points": "packed uint8" if wl["zp"] else "none",
                    "l2": f"{head['layers']} rotating weight copies (> 3x L2)",
                    "parallelism": f"column-shard x{world}" + (
-                       (" + peer-memory all-gather of Y" + (" overlapped within q/k/v and gate/up" if head["overlap"] else "")
+                       (" + peer-memory all-gather of Y" + (f" ({head['gather_mode']}: exchanges of q/k/v and gate/up "
+                                                            "joined before their consumers)" if head["overlap"] else "")
                         if head["peer"] else " + NCCL all-gather of Y") if world > 1 else ""),
                    "cuda_graphs": head["graphs"], "paths": head["paths"]},
         "roofline": head["roofline"], "kernels_us": head.get("kernels_us", {}),
@@ -742,7 +752,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--no-overlap", action="store_true",
-                    help="N > 1: run every all-gather on the compute stream (no overlap with independent GEMVs)")
+                    help="N > 1: run every all-gather right after its own GEMV (same as --gather-mode inline)")
+    ap.add_argument("--gather-mode", choices=["defer", "stream", "inline"], default="defer",
+                    help="N > 1: order of the peer-memory exchanges within a step (see Runner._build)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="omit the config-4 prefill object")

@@ -220,9 +220,9 @@ XRGPU_API int xrgpu_device_error(int32_t device, uint32_t* code, int32_t clear);
 #define XRGPU_P2P_HANDLE_BYTES 64
 typedef struct xrgpu_p2p xrgpu_p2p;
 
-/* Allocates this rank's staging region on `device` (2 * world * slot_bytes + 4 KB, zero-filled)
- * and writes its 64-byte CUDA IPC handle to ipc_handle. slot_bytes: largest shard in bytes (a
- * multiple of 16). */
+/* Allocates this rank's staging region on `device` (4 KB of flags, 2 * world * slot_bytes of shard
+ * staging and 2 * world * 2 * min(slot_bytes, 1 MiB) of word staging, zero-filled) and writes its
+ * 64-byte CUDA IPC handle to ipc_handle. slot_bytes: largest shard in bytes (a multiple of 16). */
 XRGPU_API int xrgpu_p2p_create(int32_t device, int32_t world, int32_t rank, uint64_t slot_bytes, xrgpu_p2p** group,
                                void* ipc_handle);
 
@@ -237,6 +237,28 @@ XRGPU_API int xrgpu_p2p_connect(xrgpu_p2p* group, const void* ipc_handles);
  * leaves code 0x401 in the device error word (xrgpu_device_error). */
 XRGPU_API int xrgpu_p2p_allgather(xrgpu_p2p* group, const void* shard, int64_t rows, int64_t shard_row_bytes,
                                   void* out, int64_t out_row_bytes, int64_t out_valid_bytes, void* stream);
+
+/* Sharded single-row MatMulNBits with the send half of the all-gather fused into the GEMV, in two
+ * enqueues. xrgpu_p2p_forward_send runs this rank's shard p (M == 1, float16, a problem the planner
+ * gives to the staged decode GEMV; p->y is ignored) writing its columns to out + rank * shard_cols
+ * and, from the same epilogue, to every other rank's word staging as epoch-tagged words.
+ * xrgpu_p2p_forward_recv then waits (bounded, 0x401 on expiry) for the other ranks' words and writes
+ * their columns into out. out: float16 [out_valid_cols], 16-byte aligned; shard_cols: columns per
+ * rank (a multiple of 8, at least p->N, 2 * shard_cols <= min(slot_bytes, 1 MiB)); out_valid_cols in
+ * ((world - 1) * shard_cols, world * shard_cols]. Each send must be followed by its receive before
+ * the group's next call of any kind (same stream, or ordered by an event); every rank makes the same
+ * sequence of calls. xrgpu_p2p_forward_supported sets *yes to 1 when send accepts (group, p,
+ * shard_cols). */
+XRGPU_API int xrgpu_p2p_forward_supported(xrgpu_p2p* group, const xrgpu_mmnb_problem* p, int64_t shard_cols,
+                                          int32_t* yes);
+XRGPU_API int xrgpu_p2p_forward_send(xrgpu_p2p* group, const xrgpu_mmnb_problem* p, int64_t shard_cols, void* out,
+                                     void* stream);
+XRGPU_API int xrgpu_p2p_forward_recv(xrgpu_p2p* group, int64_t shard_cols, void* out, int64_t out_valid_cols,
+                                     void* stream);
+/* The receives of up to 8 groups (each after its own send) in one kernel, e.g. the projections
+ * that share one input; groups[k] with shard_cols[k], outs[k] and out_valid_cols[k] as above. */
+XRGPU_API int xrgpu_p2p_forward_recv_many(int32_t count, xrgpu_p2p* const* groups, const int64_t* shard_cols,
+                                          void* const* outs, const int64_t* out_valid_cols, void* stream);
 
 /* Unmaps the peers' regions and frees this rank's. Call only after every rank has finished its
  * last all-gather on the group (synchronise, then a host barrier). */

@@ -153,6 +153,9 @@ def _peer_rank(rank, world, port, results):
             mods.append(peer)
             assert peer.uses_peer_gather(M) and not nccl.uses_peer_gather(M)
             ok = True
+            if M == 1:  # single-row float16 decode shards take the fused GEMV send
+                peer(d(a))
+                ok &= peer._fused_ok is not None and peer._fused_ok[1]
             # repeated calls: the epochs advance and the double-buffered staging alternates
             for rep in range(5):
                 x = d(a) * (1.0 + 0.25 * rep)
@@ -199,6 +202,102 @@ def test_peer_allgather_two_gpus_matches_nccl():
     results = manager.dict()
     mp.start_processes(_peer_rank, args=(2, _free_port(), results), nprocs=2, start_method="spawn")
     assert all(results.get((r, i), False) for r in range(2) for i in range(4)), dict(results)
+
+
+# ----------------------------------------------------------------- fused GEMV send, mixed with other calls
+# (K, N, block_size, zero points): shards of 2048, 504 and 1024 columns on one shared group
+FUSED_SPECS = [(4096, 4096, 32, "packed"), (4096, 1008, 64, None), (14336, 2048, 32, "packed")]
+
+
+def _fused_rank(rank, world, port, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    group = None
+    try:
+        from xrgpu_b200 import functional as F
+        from xrgpu_b200.p2p import PeerAllGather
+        F.device_error(rank, clear=True)
+        group = PeerAllGather(1 << 20)
+        d = lambda x: None if x is None else torch.from_numpy(x).cuda()  # noqa: E731
+        fused, plain, acts = [], [], []
+        for i, (K, N, bs, zk) in enumerate(FUSED_SPECS):
+            a, b, s, zp, bb = _case(300 + i, 4, K, N, bs, zk, True)
+            fused.append(ShardedMatMulNBits(d(b), d(s), d(zp), d(bb), K=K, N=N, block_size=bs, peer_group=group))
+            plain.append(ShardedMatMulNBits(d(b), d(s), d(zp), d(bb), K=K, N=N, block_size=bs, peer_gather=False))
+            acts.append(d(a))
+        ok = True
+        for rep in range(3):  # fused calls of three shard sizes, each followed by a 4-row call (a
+            for f, p, a in zip(fused, plain, acts):  # separate all-gather) on the same group
+                x1 = a[:1] * (1.0 + 0.5 * rep)
+                ok &= torch.equal(f(x1), p(x1)) and bool(f._fused_ok[1])
+                ok &= torch.equal(f(a), p(a))
+        side = torch.cuda.Stream()
+        for rep in range(2):  # overlapped: receives on a side stream, the next send ordered after them
+            ys = [f(a[1:2] * (0.5 + rep), gather_stream=side) for f, a in zip(fused, acts)]
+            for f in fused:
+                f.wait_gather()
+            ok &= all(torch.equal(y, p(a[1:2] * (0.5 + rep))) for y, p, a in zip(ys, plain, acts))
+        # deferred: the receive is enqueued by wait_gather on the joining stream
+        for rep in range(2):
+            for f, p, a in zip(fused, plain, acts):
+                x1 = a[3:4] * (1.5 + rep)
+                y = f(x1, defer=True)
+                f.wait_gather()
+                ok &= torch.equal(y, p(x1))
+        # deferred sends of three modules with their own groups, received by one kernel
+        own = [ShardedMatMulNBits(f.b, f.scales, f.zero_points, f.bias, K=f.K, N=f.N, block_size=f.block_size,
+                                  _presharded=True) for f in fused]
+        for rep in range(3):
+            xs = [a[rep:rep + 1] * (0.75 + rep) for a in acts]
+            ys = [m(x, defer=True) for m, x in zip(own, xs)]
+            ShardedMatMulNBits.wait_gather_all(own)
+            ok &= all(torch.equal(y, p(x)) for y, p, x in zip(ys, plain, xs))
+        for m in own:
+            m.close()
+        # two fused sends on one group without the first one's receive in between are refused
+        fused[0](acts[0][:1], defer=True)
+        try:
+            fused[1](acts[1][:1], defer=True)
+            ok = False
+        except RuntimeError:
+            pass
+        fused[0].wait_gather()
+        # captured in a CUDA graph with its receive, replayed with new inputs
+        x_in = acts[0][:1].clone()
+        y_out = torch.empty((1, FUSED_SPECS[0][1]), dtype=torch.float16, device="cuda")
+        fused[0](x_in, out=y_out)
+        torch.cuda.synchronize()
+        s_ = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s_):
+            with torch.cuda.graph(g, stream=s_):
+                fused[0](x_in, out=y_out)
+        for rep in range(4):
+            x_in.copy_(acts[0][2:3] * (0.25 + rep))
+            g.replay()
+            torch.cuda.synchronize()
+            ok &= torch.equal(y_out, plain[0](x_in))
+        del g
+        torch.cuda.synchronize()
+        results[rank] = bool(ok) and F.device_error(rank) == 0
+    finally:
+        if group is not None:
+            group.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_fused_gemv_send_two_gpus_matches_nccl():
+    """Single-row calls whose GEMV sends its columns to the other rank itself (flag-in-word words)
+    and a receive kernel assembles Y: bit-exact against NCCL's all-gather of the same shards, on one
+    group shared with separate all-gathers of other sizes, overlapped, and replayed in a graph."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(_fused_rank, args=(2, _free_port(), results), nprocs=2, start_method="spawn")
+    assert results.get(0) and results.get(1), dict(results)
 
 
 # ----------------------------------------------------------------- shards of changing size on one group

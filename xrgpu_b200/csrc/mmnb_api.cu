@@ -235,6 +235,8 @@ int problem_from_c(const xrgpu_mmnb_problem* c, Problem* p, bool need_y) {
 }  // namespace
 
 // ---------------------------------------------------------------- shared with the family operators
+int problem_from_api(const xrgpu_mmnb_problem* c, Problem* p, bool need_y) { return problem_from_c(c, p, need_y); }
+
 int select_path(const Problem& p, int forced) {
   if (forced == kPathGeneric) return kPathGeneric;
   if (forced == kPathGemv) return gemv_supported(p) ? kPathGemv : -1;

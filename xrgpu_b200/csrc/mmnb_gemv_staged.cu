@@ -60,7 +60,30 @@ struct StagedParams {
   int tiles, upt;        // 16-column tiles; units per tile (K / 128)
   int sb, zb;            // scale / zero-point bytes per row per window
   int slot_bytes;        // bytes of one stage: weights, scales, zero points
+  StagedPush push;       // sharded form: output columns also sent to the other ranks (world 0: off)
 };
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_volatile_u64(void* p, uint64_t v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Columns (n, n + 1) of this rank's shard as one word (float16 bits of n | bits of n + 1 << 16 |
+// epoch << 32) into words[e & 1][rank] of every other rank, at byte 4 n: the layout of the peer
+// all-gather's flag-in-word form, whose receive kernel takes the words. One 64-bit store each, so
+// the receiver sees data and epoch together; no fence is needed. Columns at or past the shard
+// width (ragged last tile) are not sent.
+__device__ __forceinline__ void push_pair(const StagedPush& q, uint32_t e, int n, uint32_t two) {
+  if (n >= q.cols) return;
+  const int64_t off = q.words_off + (static_cast<int64_t>(e & 1u) * q.world + q.rank) * q.ll_bytes + 4 * static_cast<int64_t>(n);
+  const uint64_t w = (static_cast<uint64_t>(e) << 32) | two;
+  for (int r = 0; r < q.world; ++r)
+    if (r != q.rank) st_volatile_u64(q.region[r] + off, w);
+}
 
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
@@ -272,6 +295,10 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_staged_kernel(const _
 #pragma unroll
   for (int j = 0; j < kNst - 1; ++j) issue();
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Sharded form: this call's epoch, one past the value the previous call's receive left (read
+  // only now, after the previous kernel in the stream has completed).
+  const bool pushing = p.push.world > 1;
+  const uint32_t push_e = pushing ? ld_volatile_u32(p.push.epoch) + 1u : 0u;
 
   for (int i = threadIdx.x; i < kZeroRegion / 16; i += kThreads) sts128(s_base + 16 * i, make_uint4(0u, 0u, 0u, 0u));
   {  // Activations: up to eight 16-byte loads per thread are in flight before any is used, so staging
@@ -360,12 +387,14 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_staged_kernel(const _
     }
   };
 
-  auto store = [&](int n, float v) {
-    if (n < p.N) {
-      v *= 16777216.f;  // 2^24
-      if (p.bias) v += __half2float(p.bias[n]);
-      p.y[n] = __float2half_rn(v);
-    }
+  // Output column n from its scaled sum: float16 bits (bias added for columns inside N).
+  auto half_bits = [&](int n, float v) -> uint32_t {
+    v *= 16777216.f;  // 2^24
+    if (p.bias && n < p.N) v += __half2float(p.bias[n]);
+    return __half_as_ushort(__float2half_rn(v));
+  };
+  auto put = [&](int n, uint32_t h) {
+    if (n < p.N) p.y[n] = __ushort_as_half(static_cast<unsigned short>(h));
   };
   // A finished segment of this warp's range inside `tile`: stored directly when the warp covered
   // the whole tile, otherwise kept in shared memory (slot 0: the warp's first tile, 1: its last)
@@ -376,9 +405,18 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_staged_kernel(const _
     tot1 += __shfl_xor_sync(0xffffffffu, tot1, 1);
     tot1 += __shfl_xor_sync(0xffffffffu, tot1, 2);
     if (whole) {
+      const int n0 = tile * kRows + g;
+      const uint32_t h0 = half_bits(n0, tot0), h1 = half_bits(n0 + 8, tot1);
       if (c == 0) {
-        store(tile * kRows + g, tot0);
-        store(tile * kRows + g + 8, tot1);
+        put(n0, h0);
+        put(n0 + 8, h1);
+      }
+      if (pushing) {  // lane 4g + 4 holds column g + 1 (and g + 9)
+        const uint32_t o0 = __shfl_down_sync(0xffffffffu, h0, 4), o1 = __shfl_down_sync(0xffffffffu, h1, 4);
+        if (c == 0 && (g & 1) == 0) {
+          push_pair(p.push, push_e, n0, h0 | (o0 << 16));
+          push_pair(p.push, push_e, n0 + 8, h1 | (o1 << 16));
+        }
       }
     } else if (c == 0) {
       float* mine = red + (warp * 2 + (first ? 0 : 1)) * kRows;
@@ -392,10 +430,15 @@ __global__ void __launch_bounds__(kThreads, kMinCtas) gemv_staged_kernel(const _
     const int qa = owner_of(t0, base, rem), qb = owner_of(t0 + p.upt - 1, base, rem);
     if (qb != warp || qa == qb) return;
     const int qa_slot = range_lo(qa, base, rem) < t0 ? 1 : 0;  // the tile is qa's last when qa began before it
-    if (lane < kRows) {
-      float v = 0.f;
+    float v = 0.f;
+    if (lane < kRows)
       for (int qq = qa; qq <= qb; ++qq) v += red[(qq * 2 + (qq == qa ? qa_slot : 0)) * kRows + lane];
-      store(tile * kRows + lane, v);
+    const int n = tile * kRows + lane;
+    const uint32_t h = half_bits(n, v);
+    if (lane < kRows) put(n, h);
+    if (pushing) {
+      const uint32_t o = __shfl_down_sync(0xffffffffu, h, 1);
+      if (lane < kRows && (lane & 1) == 0) push_pair(p.push, push_e, n, h | (o << 16));
     }
   };
 
@@ -500,7 +543,9 @@ bool gemv_staged_supported(const Problem& p) {
   return staged_smem(p) <= static_cast<size_t>(kMaxSmem);
 }
 
-cudaError_t launch_gemv_staged(const Problem& p, cudaStream_t stream) {
+cudaError_t launch_gemv_staged(const Problem& p, cudaStream_t stream) { return launch_gemv_staged_push(p, nullptr, stream); }
+
+cudaError_t launch_gemv_staged_push(const Problem& p, const StagedPush* push, cudaStream_t stream) {
   if (p.N == 0) return cudaSuccess;
   const int grid = staged_grid(p);
   StagedParams gp{};
@@ -522,6 +567,7 @@ cudaError_t launch_gemv_staged(const Problem& p, cudaStream_t stream) {
   gp.sb = sb;
   gp.zb = zb;
   gp.slot_bytes = (kStageWBytes + meta + 255) & ~255;
+  if (push) gp.push = *push;
   const size_t smem = staged_smem(p);
   switch (p.bs) {
     case 32: return launch_staged_bs<32>(p, gp, grid, smem, stream);

@@ -5,6 +5,8 @@
 #include <cstdint>
 #include <string>
 
+#include "xrgpu_mmnb.h"
+
 namespace xrgpu {
 
 enum ZpKind : int { kZpNone = 0, kZpF32 = 1, kZpF16 = 2, kZpPacked = 3 };
@@ -45,6 +47,16 @@ cudaError_t launch_gemv_m1(const Problem& p, cudaStream_t s);
 // Its single-row form with the weights staged through shared memory by asynchronous copies.
 bool gemv_staged_supported(const Problem& p);
 cudaError_t launch_gemv_staged(const Problem& p, cudaStream_t s);
+// Sharded form of the staged GEMV (peer all-gather, flag-in-word layout): every output column
+// n < cols is also sent to each other rank r as part of the word of columns (n & ~1, n | 1), at
+// region[r] + words_off + ((e & 1) world + rank) ll_bytes + 4 (n & ~1), e = *epoch + 1.
+struct StagedPush {
+  int world, rank, cols;
+  const uint32_t* epoch;  // the group's epoch (a slot the all-gather's receive advances once per call)
+  char* region[16];       // every rank's peer-memory region, as mapped on this device
+  int64_t words_off, ll_bytes;
+};
+cudaError_t launch_gemv_staged_push(const Problem& p, const StagedPush* push, cudaStream_t s);
 
 // 4-bit prefill GEMM on tcgen05 tensor cores (sm_100a), float16 activations.
 bool gemm_supported(const Problem& p);
@@ -62,6 +74,9 @@ int api_fail(int status, const std::string& message);
 // Device error word of the current device (nonzero after a kernel's bounded wait expired).
 unsigned* device_error_word();
 cudaError_t read_device_error(uint32_t* code, bool clear);
+
+// Validates a C-ABI problem and converts it (need_y: A and Y must be given when M > 0).
+int problem_from_api(const xrgpu_mmnb_problem* c, Problem* p, bool need_y);
 
 // The planner's kernel choice for a problem (forced: a Path, kPathAuto = the planner's), -1 when a
 // forced path does not support it; its name; its scratch bytes; and its launch.

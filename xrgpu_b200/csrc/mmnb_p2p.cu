@@ -222,6 +222,7 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_ll_kernel(const __grid
   const int64_t width = valid < q.srb ? valid : q.srb;
   bool ok = true;
   for (int64_t i = lo + threadIdx.x; i < hi && ok; i += blockDim.x) {
+    if ((8 * i) % q.srb >= width) continue;  // past this block's valid columns: nothing to take
     uint64_t w0, w1;
     ld_ll_pair(src + 16 * i, w0, w1);
     if (static_cast<uint32_t>(w0 >> 32) != e || static_cast<uint32_t>(w1 >> 32) != e) {
@@ -237,7 +238,6 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_ll_kernel(const __grid
       if (!ok) break;
     }
     const int64_t m = (8 * i) / q.srb, j = 8 * i - m * q.srb;
-    if (j >= width) continue;
     char* o = q.out + block_off + m * q.orb + j;
     const uint32_t d0 = static_cast<uint32_t>(w0), d1 = static_cast<uint32_t>(w1);
     if (j + 8 <= width) {
@@ -249,6 +249,87 @@ __global__ void __launch_bounds__(kThreads) p2p_allgather_ll_kernel(const __grid
   __syncthreads();  // every thread has read epoch_s
   if (threadIdx.x == 0)
     for (int slot = c; slot < kMaxChunks; slot += q.chunks) epoch[slot] = e;  // every slot once per call
+}
+
+// Receive side of the fused form (the decode GEMV sent the words), for up to kMaxRecvGroups groups in
+// one launch. Group gi has (world - 1) * chunks CTAs; CTA (p, c) takes pairs [lo, hi) of peer p's
+// single-row block from this rank's words[e & 1][p] and writes them into Y. The epoch slot and the
+// first pair of both parities are loaded together, so the epoch costs no extra round trip.
+constexpr int kMaxRecvGroups = 8;
+struct RecvGroup {
+  const char* words;  // this rank's words[0][0] (region + words offset)
+  uint32_t* epoch;    // the group's epoch slots [XRGPU_P2P_MAX_WORLD][kMaxChunks]
+  char* out;          // Y: one row, rank q's block at byte q * srb
+  int64_t srb, ovb, ll_bytes;
+  int world, rank, chunks, first_cta;
+};
+struct RecvManyParams {
+  RecvGroup g[kMaxRecvGroups];
+  int count;
+  unsigned* err;
+};
+
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kSmallThreads) p2p_recv_many_kernel(const __grid_constant__ RecvManyParams P) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  int gi = 0;
+  while (gi + 1 < P.count && static_cast<int>(blockIdx.x) >= P.g[gi + 1].first_cta) ++gi;
+  const RecvGroup& G = P.g[gi];
+  const int local = static_cast<int>(blockIdx.x) - G.first_cta;
+  int p = local / G.chunks;
+  const int c = local % G.chunks;
+  if (p >= G.rank) ++p;  // peers only
+  const int64_t pairs = G.srb / 8;
+  const int64_t per = (pairs + G.chunks - 1) / G.chunks;
+  const int64_t lo = per * c < pairs ? per * c : pairs, hi = per * (c + 1) < pairs ? per * (c + 1) : pairs;
+  const int64_t block_off = static_cast<int64_t>(p) * G.srb;
+  const int64_t valid = G.ovb - block_off;
+  const int64_t width = valid < G.srb ? valid : G.srb;
+  uint32_t* epoch = G.epoch + p * kMaxChunks;
+  const char* par0 = G.words + static_cast<int64_t>(p) * G.ll_bytes;
+  const char* par1 = G.words + (static_cast<int64_t>(G.world) + p) * G.ll_bytes;
+  int64_t i = lo + threadIdx.x;
+  uint64_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+  if (i < hi && 8 * i < width) {
+    ld_ll_pair(par0 + 16 * i, a0, a1);
+    ld_ll_pair(par1 + 16 * i, b0, b1);
+  }
+  const uint32_t e = ld_volatile_u32(epoch + c) + 1u;
+  const char* src = (e & 1u) ? par1 : par0;
+  uint64_t w0 = (e & 1u) ? b0 : a0, w1 = (e & 1u) ? b1 : a1;
+  bool ok = true, first = true;
+  for (; i < hi && ok; i += blockDim.x, first = false) {
+    if (8 * i >= width) continue;  // past this block's valid columns: never sent
+    if (!first) ld_ll_pair(src + 16 * i, w0, w1);
+    if (static_cast<uint32_t>(w0 >> 32) != e || static_cast<uint32_t>(w1 >> 32) != e) {
+      const uint64_t start = global_timer_ns();
+      do {
+        if (global_timer_ns() - start > kWaitLimitNs) {
+          record_device_error(P.err, kErrPeerWait);
+          ok = false;
+          break;
+        }
+        ld_ll_pair(src + 16 * i, w0, w1);
+      } while (static_cast<uint32_t>(w0 >> 32) != e || static_cast<uint32_t>(w1 >> 32) != e);
+      if (!ok) break;
+    }
+    char* o = G.out + block_off + 8 * i;
+    const uint32_t d0 = static_cast<uint32_t>(w0), d1 = static_cast<uint32_t>(w1);
+    if (8 * i + 8 <= width) {
+      *reinterpret_cast<uint2*>(o) = make_uint2(d0, d1);
+    } else {  // ragged end of the last block
+      for (int64_t t = 0; t < width - 8 * i; ++t) o[t] = static_cast<char>((t < 4 ? d0 >> (8 * t) : d1 >> (8 * (t - 4))) & 0xff);
+    }
+  }
+  __syncthreads();  // every thread has read the epoch slot
+  if (threadIdx.x == 0)
+    for (int slot = c; slot < kMaxChunks; slot += G.chunks) epoch[slot] = e;  // every slot once per call
 }
 
 }  // namespace
@@ -377,6 +458,141 @@ int xrgpu_p2p_allgather(xrgpu_p2p* g, const void* shard, int64_t rows, int64_t s
   cudaSetDevice(prev);
   if (e != cudaSuccess) return api_fail(XRGPU_RUNTIME_ERROR, std::string("peer all-gather launch failed: ") + cudaGetErrorString(e));
   return XRGPU_OK;
+}
+
+}  // extern "C"
+
+namespace xrgpu {
+namespace {
+
+// Checks for the fused form; on success *prob is this rank's problem with y = out + rank * shard_cols.
+int fused_check(xrgpu_p2p* g, const xrgpu_mmnb_problem* c, int64_t shard_cols, void* out, Problem* prob,
+                std::string* why) {
+  if (!g || !c) { *why = "null group or problem"; return XRGPU_INVALID_ARGUMENT; }
+  for (int p = 0; p < g->world; ++p)
+    if (!g->peers[p]) { *why = "group not connected (xrgpu_p2p_connect)"; return XRGPU_INVALID_ARGUMENT; }
+  if (g->world < 2) { *why = "the fused form needs at least two ranks"; return XRGPU_INVALID_ARGUMENT; }
+  if (shard_cols <= 0 || shard_cols % 8 || shard_cols < c->N || static_cast<uint64_t>(4 * shard_cols) > g->ll_bytes) {
+    *why = "shard_cols must be a multiple of 8, at least N, with 2 * shard_cols <= min(slot_bytes, 1 MiB)";
+    return XRGPU_INVALID_ARGUMENT;
+  }
+  if (reinterpret_cast<uintptr_t>(out) % 16) { *why = "out must be 16-byte aligned"; return XRGPU_INVALID_ARGUMENT; }
+  xrgpu_mmnb_problem mine = *c;
+  mine.y = out ? static_cast<char*>(out) + 2 * shard_cols * g->rank : nullptr;
+  mine.ldy = 0;
+  const int st = problem_from_api(&mine, prob, out != nullptr);
+  if (st) { *why = "invalid problem"; return st; }
+  if (!(prob->f16 && prob->M == 1 && select_path(*prob, c->path) == kPathGemv && gemv_staged_supported(*prob))) {
+    *why = "the fused form runs single-row float16 problems of the staged decode GEMV only";
+    return XRGPU_INVALID_ARGUMENT;
+  }
+  return XRGPU_OK;
+}
+
+}  // namespace
+}  // namespace xrgpu
+
+extern "C" {
+
+int xrgpu_p2p_forward_supported(xrgpu_p2p* g, const xrgpu_mmnb_problem* p, int64_t shard_cols, int32_t* yes) {
+  using namespace xrgpu;
+  if (!yes) return api_fail(XRGPU_INVALID_ARGUMENT, "null result pointer");
+  *yes = 0;
+  if (!g || !p) return api_fail(XRGPU_INVALID_ARGUMENT, "null group or problem");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(g->device);
+  Problem prob;
+  std::string why;
+  // a 16-byte aligned stand-in for out: only the problem's own pointers are checked
+  *yes = fused_check(g, p, shard_cols, reinterpret_cast<void*>(uintptr_t{256}), &prob, &why) == XRGPU_OK ? 1 : 0;
+  cudaSetDevice(prev);
+  return XRGPU_OK;
+}
+
+int xrgpu_p2p_forward_send(xrgpu_p2p* g, const xrgpu_mmnb_problem* c, int64_t shard_cols, void* out, void* stream) {
+  using namespace xrgpu;
+  if (!out) return api_fail(XRGPU_INVALID_ARGUMENT, "null output");
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (g) cudaSetDevice(g->device);
+  Problem prob;
+  std::string why;
+  int st = fused_check(g, c, shard_cols, out, &prob, &why);
+  if (st) {
+    cudaSetDevice(prev);
+    return api_fail(st, why);
+  }
+  StagedPush push{};
+  push.world = g->world;
+  push.rank = g->rank;
+  push.cols = static_cast<int>(shard_cols);
+  push.epoch = g->epoch + ((g->rank + 1) % g->world) * kMaxChunks;  // slot 0 of another rank (all equal)
+  for (int p = 0; p < g->world; ++p) push.region[p] = g->peers[p];
+  push.words_off = kFlagBytes + 2 * static_cast<int64_t>(g->world) * static_cast<int64_t>(g->slot_bytes);
+  push.ll_bytes = static_cast<int64_t>(g->ll_bytes);
+  prob.err = device_error_word();
+  const cudaError_t e = launch_gemv_staged_push(prob, &push, static_cast<cudaStream_t>(stream));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return api_fail(XRGPU_RUNTIME_ERROR, std::string("fused GEMV launch failed: ") + cudaGetErrorString(e));
+  return XRGPU_OK;
+}
+
+int xrgpu_p2p_forward_recv_many(int32_t count, xrgpu_p2p* const* groups, const int64_t* shard_cols, void* const* outs,
+                                const int64_t* out_valid_cols, void* stream) {
+  using namespace xrgpu;
+  if (count < 1 || count > kMaxRecvGroups || !groups || !shard_cols || !outs || !out_valid_cols)
+    return api_fail(XRGPU_INVALID_ARGUMENT, "need 1 to 8 groups with their shard widths, outputs and valid widths");
+  RecvManyParams P{};
+  P.count = count;
+  int ctas = 0;
+  for (int k = 0; k < count; ++k) {
+    xrgpu_p2p* g = groups[k];
+    const int64_t S = shard_cols[k], valid = out_valid_cols[k];
+    if (!g || !outs[k]) return api_fail(XRGPU_INVALID_ARGUMENT, "null group or output");
+    if (g->device != groups[0]->device) return api_fail(XRGPU_INVALID_ARGUMENT, "groups of one receive must share a device");
+    for (int p = 0; p < g->world; ++p)
+      if (!g->peers[p]) return api_fail(XRGPU_INVALID_ARGUMENT, "group not connected (xrgpu_p2p_connect)");
+    if (g->world < 2 || S <= 0 || S % 8 || static_cast<uint64_t>(4 * S) > g->ll_bytes || valid <= (g->world - 1) * S ||
+        valid > g->world * S || reinterpret_cast<uintptr_t>(outs[k]) % 16)
+      return api_fail(XRGPU_INVALID_ARGUMENT,
+                      "need world >= 2, shard_cols a multiple of 8 within the word staging, "
+                      "(world-1)*shard_cols < out_valid_cols <= world*shard_cols and a 16-byte aligned out");
+    RecvGroup& G = P.g[k];
+    G.words = g->local + kFlagBytes + 2 * static_cast<int64_t>(g->world) * static_cast<int64_t>(g->slot_bytes);
+    G.epoch = g->epoch;
+    G.out = static_cast<char*>(outs[k]);
+    G.srb = 2 * S;
+    G.ovb = 2 * valid;
+    G.ll_bytes = static_cast<int64_t>(g->ll_bytes);
+    G.world = g->world;
+    G.rank = g->rank;
+    const int64_t per_cta = kSmallThreads * kLLPairsPerThread;
+    G.chunks = static_cast<int>(std::min<int64_t>(kMaxChunks, std::max<int64_t>(1, (G.srb / 8 + per_cta - 1) / per_cta)));
+    G.first_cta = ctas;
+    ctas += (g->world - 1) * G.chunks;
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(groups[0]->device);
+  P.err = device_error_word();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas), 1, 1);
+  cfg.blockDim = dim3(kSmallThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, p2p_recv_many_kernel, P);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return api_fail(XRGPU_RUNTIME_ERROR, std::string("peer receive launch failed: ") + cudaGetErrorString(e));
+  return XRGPU_OK;
+}
+
+int xrgpu_p2p_forward_recv(xrgpu_p2p* g, int64_t shard_cols, void* out, int64_t out_valid_cols, void* stream) {
+  return xrgpu_p2p_forward_recv_many(1, &g, &shard_cols, &out, &out_valid_cols, stream);
 }
 
 int xrgpu_p2p_destroy(xrgpu_p2p* g) {

@@ -6,6 +6,12 @@ ranks' regions; ``all_gather(shard, out)`` then enqueues one kernel on the curre
 leaves every rank's shard in ``out`` -- no NCCL call, so CUDA graphs capture it. Every rank must
 make the same sequence of calls. ``close()`` synchronises, waits for all ranks and unmaps.
 
+Fused form (single-row float16 problems of the staged decode GEMV): ``send(problem, S, out)`` runs
+this rank's GEMV, whose epilogue also writes each finished pair of output columns to every other
+rank as one epoch-tagged 8-byte word; ``recv(S, out, N)`` then waits for the other ranks' words and
+writes their columns into ``out``. A send must be followed by its receive before the group's next
+call; a send or all-gather issued on another stream than the last receive waits for it.
+
 A peer that does not arrive within 1 s makes the kernel give up, record code 0x401 in the
 device's error word and return; every rank's epochs are then out of step, so the group cannot be
 used again. ``check()`` (after synchronising) reads and clears that word and raises.
@@ -39,6 +45,9 @@ class PeerAllGather:
                                            ctypes.byref(ptr), handle))
         self._g = ptr
         self.broken = False
+        self._recv_done = None  # (stream, captured) of the last fused receive
+        self._sent = False      # a fused send is waiting for its receive
+        self._recv_seq = 0
         handles = [None] * self.world
         dist.all_gather_object(handles, handle.raw, group=group)
         try:
@@ -59,12 +68,93 @@ class PeerAllGather:
             raise RuntimeError("peer all-gather group gave up waiting for a peer earlier; close it")
         if shard.dim() != 2 or not shard.is_contiguous() or out.dim() != 2 or out.stride(1) != 1:
             raise ValueError("shard must be a contiguous [M, S] tensor and out an [M, >= N] row-major view")
+        if self._sent:
+            raise RuntimeError("peer group: a fused send is waiting for its receive (recv before the next call)")
         es = shard.element_size()
-        stream = torch.cuda.current_stream(self.device).cuda_stream
+        cur = torch.cuda.current_stream(self.device)
+        self._order_after_recv(cur)
+        stream = cur.cuda_stream
         _native.check(_native.load().xrgpu_p2p_allgather(
             self._g, ctypes.c_void_p(shard.data_ptr()), shard.shape[0], shard.shape[1] * es,
             ctypes.c_void_p(out.data_ptr()), out.stride(0) * es, valid_cols * es, ctypes.c_void_p(stream)))
         return out
+
+    # ---- fused form (single-row float16 problems of the staged decode GEMV)
+    def forward_supported(self, problem, shard_cols: int) -> bool:
+        """Whether ``send`` accepts this rank's problem (a ``_native.Problem_``) with shard_cols."""
+        if self._g is None or self.broken:
+            return False
+        yes = ctypes.c_int32(0)
+        _native.check(_native.load().xrgpu_p2p_forward_supported(self._g, ctypes.byref(problem), int(shard_cols),
+                                                                 ctypes.byref(yes)))
+        return bool(yes.value)
+
+    def send(self, problem, shard_cols: int, out: torch.Tensor) -> None:
+        """Enqueue on the current stream this rank's GEMV (``problem``, its y ignored) writing its
+        columns to out[rank * shard_cols:] and sending them to every other rank. ``recv`` must follow
+        before the group's next call; a receive left on another stream is waited for here."""
+        if self._g is None:
+            raise RuntimeError("peer all-gather group is closed")
+        if self.broken:
+            raise RuntimeError("peer all-gather group gave up waiting for a peer earlier; close it")
+        if self._sent:
+            raise RuntimeError("peer group: the previous fused send has no receive yet (recv before the next call)")
+        stream = torch.cuda.current_stream(self.device)
+        self._order_after_recv(stream)
+        self._sent = True
+        _native.check(_native.load().xrgpu_p2p_forward_send(self._g, ctypes.byref(problem), int(shard_cols),
+                                                            ctypes.c_void_p(out.data_ptr()),
+                                                            ctypes.c_void_p(stream.cuda_stream)))
+
+    def recv(self, shard_cols: int, out: torch.Tensor, valid_cols: int) -> None:
+        """Enqueue on the current stream the receive of the other ranks' columns of the last
+        ``send`` into out (bounded wait; 0x401 on expiry)."""
+        PeerAllGather.recv_many([(self, shard_cols, out, valid_cols)])
+
+    @staticmethod
+    def recv_many(items) -> None:
+        """The receives of several groups [(group, shard_cols, out, valid_cols), ...] (each after its
+        own send, all on one device) in one kernel on the current stream."""
+        groups = [it[0] for it in items]
+        for g in groups:
+            if g._g is None:
+                raise RuntimeError("peer all-gather group is closed")
+            if not g._sent:
+                raise RuntimeError("peer group: recv without a preceding fused send")
+        n = len(items)
+        arr = lambda ct, vals: (ct * n)(*vals)  # noqa: E731
+        stream = torch.cuda.current_stream(groups[0].device)
+        _native.check(_native.load().xrgpu_p2p_forward_recv_many(
+            n, arr(ctypes.c_void_p, [g._g for g in groups]), arr(ctypes.c_int64, [int(it[1]) for it in items]),
+            arr(ctypes.c_void_p, [it[2].data_ptr() for it in items]), arr(ctypes.c_int64, [int(it[3]) for it in items]),
+            ctypes.c_void_p(stream.cuda_stream)))
+        captured = torch.cuda.is_current_stream_capturing()
+        for g in groups:
+            g._sent = False
+            g._recv_seq += 1
+            g._recv_done = (stream, captured)
+
+    def _order_after_recv(self, stream) -> None:
+        """Make `stream` wait for the stream of the group's last fused receive when that is another
+        stream in the same capture state (a receive captured in another graph must have been joined
+        by the caller, e.g. ShardedMatMulNBits.wait_gather). No event is recorded when the receive
+        and the next call share a stream, so consecutive kernels keep their early launch."""
+        if self._recv_done is None or self._recv_done[0] == stream:
+            return
+        if self._recv_done[1] != torch.cuda.is_current_stream_capturing():
+            return
+        stream.wait_stream(self._recv_done[0])
+
+    def joined(self, seq: int) -> None:
+        """The caller's stream now waits for this group's receive number `seq` (``recv_seq`` after
+        it was enqueued): if no receive followed it, later calls need no further ordering."""
+        if seq == self._recv_seq:
+            self._recv_done = None
+
+    @property
+    def recv_seq(self) -> int:
+        """Number of fused receives enqueued on this group so far."""
+        return self._recv_seq
 
     PEER_WAIT_EXPIRED = 0x401
 

@@ -60,7 +60,7 @@ class ShardedMatMulNBits:
                  bias: Optional[torch.Tensor] = None, *, K: int, N: int, bits: int = 4, block_size: int,
                  group=None, compute: Optional[Callable] = None, peer_gather: Optional[bool] = None,
                  peer_max_bytes: int = 64 << 20, peer_group=None, peer_slot_bytes: int = 0,
-                 _presharded: bool = False):
+                 fuse: Optional[bool] = None, _presharded: bool = False):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -90,6 +90,14 @@ class ShardedMatMulNBits:
         self._peer = None
         self._y_buf = None        # shard buffer of the overlapped form (see forward)
         self._gather_done = None  # event of the last overlapped gather
+        # Fused form for single-row float16 calls on the staged decode GEMV: the GEMV's epilogue sends
+        # its columns to the other ranks itself and only a receive kernel remains (XRGPU_FUSED_GATHER=0
+        # turns it off, e.g. to compare with the separate all-gather).
+        self.fuse = bool(fuse) if fuse is not None else os.environ.get("XRGPU_FUSED_GATHER", "1") != "0"
+        self._fused_ok = None
+        self._fused_group = None  # group of a fused receive left on a gather stream
+        self._pending = None       # deferred exchange (forward(..., defer=True)), run by wait_gather
+        self._pending_copy = None  # (caller's out, aligned buffer) when out was not 16-byte aligned
 
     @classmethod
     def from_shard(cls, b_shard: torch.Tensor, scales_shard: torch.Tensor, zero_points_shard=None, bias_shard=None,
@@ -160,7 +168,7 @@ class ShardedMatMulNBits:
         return out
 
     def forward(self, a: torch.Tensor, out: Optional[torch.Tensor] = None,
-                gather_stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+                gather_stream: Optional[torch.cuda.Stream] = None, defer: bool = False) -> torch.Tensor:
         """Full Y [*, N] on every rank. `out` (contiguous, Y's shape) receives it without an extra
         copy when M == 1 and N is a multiple of the group size.
 
@@ -168,11 +176,21 @@ class ShardedMatMulNBits:
         local kernel, so the calling stream can go on with independent work; Y is complete once
         the caller has made its stream wait with ``wait_gather()``. The shard buffer is then this
         module's own and is reused by its next call, so call ``wait_gather()`` before calling the
-        module again. Every rank must issue its gathers in the same order on its group."""
+        module again. Every rank must issue its gathers in the same order on its group.
+
+        defer (peer-memory all-gather only): the exchange is left pending and ``wait_gather()``
+        enqueues it on the stream that joins, so independent kernels can run first on one stream
+        (no cross-stream event between them, and each kernel launches early behind the previous one);
+        Y is complete after ``wait_gather()``."""
         lead = tuple(a.shape[:-1])
         M = a.numel() // self.K
         a2 = a.reshape(M, self.K)
-        overlap = gather_stream is not None and self.world > 1 and self.uses_peer_gather(M, a.element_size())
+        if self._pending is not None:
+            raise RuntimeError("ShardedMatMulNBits: call wait_gather() for the deferred exchange before the next call")
+        fused = self._fused_form(a2)
+        if fused is not None:
+            return self._forward_fused(a2, fused, out, gather_stream, lead, defer)
+        overlap = (gather_stream is not None or defer) and self.world > 1 and self.uses_peer_gather(M, a.element_size())
         if overlap:
             key = (M, a.dtype, a.device)
             if self._y_buf is None or self._y_buf[0] != key:
@@ -192,6 +210,11 @@ class ShardedMatMulNBits:
             direct = out is not None and out.data_ptr() % 16 == 0 and (M == 1 or (out.view(M, self.N).stride(0) * es) % 16 == 0)
             dst = out.view(M, self.N) if direct else torch.empty((M, self.N), dtype=a.dtype, device=a.device)
             group = self._peer_group(M * self.S * es)
+            if defer:
+                self._pending = ("call", lambda: group.all_gather(y_local, dst, self.N))
+                if out is not None and not direct:
+                    self._pending_copy = (out.view(M, self.N), dst)
+                return out if out is not None else dst.reshape(*lead, self.N)
             if overlap:
                 ready = torch.cuda.Event()
                 ready.record()
@@ -225,11 +248,83 @@ class ShardedMatMulNBits:
             return out
         return y.reshape(*lead, self.N)
 
+    # ---- fused form: the decode GEMV sends its columns itself (peer all-gather, flag-in-word words)
+    def _fused_form(self, a2: torch.Tensor):
+        """(group, problem) when this call can run as one fused GEMV send plus a receive: more than
+        one rank, peer all-gather, one float16 row, the package's own kernel as the shard compute, and
+        a problem the staged decode GEMV takes (asked of the library once per module)."""
+        if (self.world < 2 or not self.fuse or a2.shape[0] != 1 or a2.dtype != torch.float16
+                or self.compute is not F.matmul_nbits or not self.uses_peer_gather(1, 2)):
+            return None
+        group = self._peer_group(self.S * 2)
+        prob = F._problem(a2, self.b, self.scales, self.zero_points, self.bias, None, K=self.K,
+                          N=self.n1 - self.n0, bits=self.bits, block_size=self.block_size, path="auto")
+        key = (id(group), a2.data_ptr() % 16 == 0)
+        if self._fused_ok is None or self._fused_ok[0] != key:
+            self._fused_ok = (key, group.forward_supported(prob, self.S))
+        return (group, prob) if self._fused_ok[1] else None
+
+    def _forward_fused(self, a2, fused, out, gather_stream, lead, defer=False):
+        group, prob = fused
+        direct = out is not None and out.is_contiguous() and out.data_ptr() % 16 == 0
+        dst = out.view(1, self.N) if direct else torch.empty((1, self.N), dtype=a2.dtype, device=a2.device)
+        group.send(prob, self.S, dst)
+        if defer:
+            self._pending = ("recv", (group, self.S, dst, self.N))
+            if out is not None and not direct:
+                self._pending_copy = (out.view(1, self.N), dst)
+            return out if out is not None else dst.reshape(*lead, self.N)
+        if gather_stream is not None:
+            ready = torch.cuda.Event()
+            ready.record()
+            gather_stream.wait_event(ready)
+            with torch.cuda.stream(gather_stream):
+                group.recv(self.S, dst, self.N)
+                self._gather_done = torch.cuda.Event()
+                self._gather_done.record()
+            self._fused_group = (group, group.recv_seq)
+        else:
+            group.recv(self.S, dst, self.N)
+        if out is not None and not direct:
+            if gather_stream is not None:
+                self.wait_gather()
+            out.view(1, self.N).copy_(dst)
+            return out
+        return out if out is not None else dst.reshape(*lead, self.N)
+
     def wait_gather(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         """Make `stream` (default: the current one) wait for the last gather issued on a
-        gather_stream; a no-op when none is pending."""
+        gather_stream, or enqueue a deferred exchange on it; a no-op when none is pending."""
+        if self._pending is not None:
+            ShardedMatMulNBits.wait_gather_all([self], stream)
+            return
         if self._gather_done is not None:
             (stream or torch.cuda.current_stream()).wait_event(self._gather_done)
+            if self._fused_group is not None:
+                self._fused_group[0].joined(self._fused_group[1])
+                self._fused_group = None
             self._gather_done = None
+
+    @staticmethod
+    def wait_gather_all(mods, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """``wait_gather()`` of several modules; their deferred fused receives (at most 8 per kernel)
+        run as one kernel on `stream` (default: the current one)."""
+        from .p2p import PeerAllGather
+        with torch.cuda.stream(stream or torch.cuda.current_stream()):
+            recvs = [m for m in mods if m._pending is not None and m._pending[0] == "recv"]
+            for i in range(0, len(recvs), 8):
+                PeerAllGather.recv_many([m._pending[1] for m in recvs[i:i + 8]])
+            for m in mods:
+                if m._pending is None:
+                    m.wait_gather()
+                    continue
+                kind, what = m._pending
+                m._pending = None
+                if kind == "call":
+                    what()
+                if m._pending_copy is not None:
+                    dst_out, src = m._pending_copy
+                    m._pending_copy = None
+                    dst_out.copy_(src)
 
     __call__ = forward
