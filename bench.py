@@ -20,7 +20,9 @@ so every step streams its weights from HBM (config: "l2": "rotating weight copie
 
 The line for the default workload also carries a "prefill" object: config 4 (M=2048, K=4096,
 N=14336, bs 64, no zero points) measured in the same run with its own roofline, e2e and CPU
-baseline, so both halves of the metric are in one record.
+baseline, so both halves of the metric are in one record. On one GPU it also carries
+"batched_decode": config 3 (M = 4, 16, 64; K=4096, N=14336, bs 128, packed zero points), each
+with its step time and roofline.
 
 Multi-GPU (torchrun, one process per GPU, NCCL): the headline is weak scaling -- every rank owns a
 contiguous 1/N slice of each projection's output columns of an N-times-wider layer (per-GPU work
@@ -630,6 +632,15 @@ def run_ours(args):
                                 workload="prefill_m2048", M=2048, K=4096, N=14336, block_size=64, zero_points="none",
                                 e2e=pre.get("e2e"), cpu_baseline=pre.get("cpu_baseline"),
                                 kernels_us=pre.get("kernels_us"), parity=pre.get("parity"))
+    if args.workload == "llama3_8b_decode" and world == 1 and not args.no_batched:
+        batched = {}
+        for name in ("batched_decode_m4", "batched_decode_m16", "batched_decode_m64"):
+            r = measure(name, args, world, rank, local, device, mode="weak")
+            w = WORKLOADS[name]
+            batched[name] = dict(value=round(r["value"], 2), unit=r["unit"], ms_per_step=round(r["step_ms"], 5),
+                                 M=w["M"], K=4096, N=14336, block_size=w["bs"], zero_points="packed uint8",
+                                 paths=r["paths"], roofline=r["roofline"], kernels_us=r.get("kernels_us"))
+        extra["batched_decode"] = batched
     if world > 1 and not args.no_strong:
         strong = {}
         for name in ("llama3_8b_decode", "prefill_m2048"):
@@ -759,6 +770,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="omit the config-4 prefill object")
     ap.add_argument("--no-strong", action="store_true", help="N > 1: omit the fixed-problem (strong) objects")
+    ap.add_argument("--no-batched", action="store_true", help="omit the config-3 batched-decode objects (N = 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
