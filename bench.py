@@ -372,18 +372,36 @@ class Runner:
         torch.cuda.synchronize()
         return graphs
 
+    def capture_seq(self, fn, layers):
+        """One CUDA graph of fn(layer) for every layer in `layers`, in order."""
+        import torch
+        s = torch.cuda.Stream(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for layer in layers:
+                    fn(layer)
+        torch.cuda.synchronize()
+        return g
+
     def timed(self, fn, count, graphs, steps, warmup, clocks=None):
         """Device time per step (ms, max over ranks) of `steps` steps after `warmup` untimed ones,
-        bracketed by a barrier and a synchronize on both sides."""
+        bracketed by a barrier and a synchronize on both sides. With graphs, the timed steps are one
+        CUDA graph holding all of them (step i on weight copy i mod count), so a step's time is the
+        device's and not the host's launch rate; the warm-up replays its own graph."""
         import torch
 
+        seq = {}
+        if graphs:
+            seq[max(3, warmup)] = self.capture_seq(fn, [i % count for i in range(max(3, warmup))])
+            seq[steps] = seq.get(steps) or self.capture_seq(fn, [i % count for i in range(steps)])
+
         def run(n, offset=0):
+            if graphs:
+                seq[n].replay()
+                return
             for i in range(n):
-                layer = (offset + i) % count
-                if graphs:
-                    graphs[layer].replay()
-                else:
-                    fn(layer)
+                fn((offset + i) % count)
 
         run(max(3, warmup))
         barrier(self.world)
@@ -586,10 +604,9 @@ def measure(name, args, world, rank, local, device, *, mode="weak", headline=Fal
     res = dict(workload=name, config=wl["config"], mode=mode, layers=runner.layers, paths=runner.paths)
     if world > 1:
         res["parity"] = runner.parity()
-    graphs = runner.capture(runner.step, runner.layers) if runner.graphable else None
+    graphs = runner.graphable
     clocks = ClockSampler(local) if headline else None
     step_ms, clock = runner.timed(runner.step, runner.layers, graphs, args.steps, args.warmup, clocks)
-    del graphs
     res.update(step_ms=step_ms, value=runner.value_of(step_ms), clocks=clock,
                unit="GB/s" if wl["kind"] == "decode" else "TFLOP/s",
                metric="MatMulNBits decode GB/s" if wl["kind"] == "decode" else "MatMulNBits prefill TFLOP/s",
@@ -600,9 +617,8 @@ def measure(name, args, world, rank, local, device, *, mode="weak", headline=Fal
         res["kernels_us"] = runner.kernel_times()
     if mode == "strong" and world > 1:
         runner.ys_full = {n: torch.empty_like(y) for n, y in runner.ys.items()}
-        g1 = runner.capture(runner.step_full, len(runner.full)) if not args.no_graphs else None
+        g1 = not args.no_graphs
         one_ms, _ = runner.timed(runner.step_full, len(runner.full), g1, args.steps, args.warmup)
-        del g1
         res.update(one_gpu_ms=one_ms, speedup=one_ms / step_ms, efficiency=one_ms / step_ms / world)
     if not args.no_e2e and mode == "weak":
         res["e2e"] = runner.e2e(args.steps, args.warmup)

@@ -180,6 +180,45 @@ def test_gemv_writes_strided_output_slice(F):
     assert within_baseline_tol(out[:, N:2 * N], ref)[0]
 
 
+# Multi-row staged GEMV (block size 128 / 256, K % 512 == 0): M = 1..16 with one or two 8-row
+# activation tiles, ragged N, every zero-point form, strided output rows, full config-3 width.
+MR_SHAPES = [
+    # (M, K, N, bs)
+    (2, 4096, 1000, 128), (5, 2048, 777, 256), (8, 4096, 14336, 128), (9, 1024, 300, 128),
+    (16, 4096, 14336, 128), (12, 1024, 64, 256), (1, 4096, 2048, 128), (16, 512, 17, 128),
+]
+
+
+@pytest.mark.parametrize("M,K,N,bs", MR_SHAPES)
+@pytest.mark.parametrize("zp_kind", [None, "float16", "packed", "frac"])
+def test_gemv_multirow_staged_matches_oracle(F, M, K, N, bs, zp_kind):
+    rng = np.random.default_rng(M * 977 + K + N + bs)
+    zk = {"float16": np.float16}.get(zp_kind, zp_kind)
+    a, b, s, zp, bias = make(rng, M, K, N, 4, bs, np.float16, zk, bias=(N % 2 == 0))
+    y = run_gpu(F, a, b, s, zp, bias, K=K, N=N, bits=4, bs=bs, path="gemv")
+    cols = slice(0, min(N, 2048))  # oracle on a column sample at full width
+    ref = O.matmul_nbits(a, b, s, zp, bias, K=K, N=N, bits=4, block_size=bs, columns=cols)
+    ok, st = within_baseline_tol(y[:, cols], ref)
+    assert ok, st
+    err = np.abs(y[:, cols].astype(np.float64) - ref.astype(np.float64))
+    assert np.all(err <= 2e-3 * np.abs(ref.astype(np.float64)) + 1e-3 * np.abs(ref).max() + 1e-6)
+    y2 = run_gpu(F, a, b, s, zp, bias, K=K, N=N, bits=4, bs=bs, path="gemv")
+    assert np.array_equal(y, y2)  # fixed-order sums of cut tiles
+
+
+def test_gemv_multirow_staged_strided_output_rows(F):
+    rng = np.random.default_rng(8)
+    M, K, N, bs = 6, 2048, 96, 128
+    a, b, s, zp, bias = make(rng, M, K, N, 4, bs, np.float16, "packed", bias=True)
+    big = torch.full((M, 3 * N), 7.0, dtype=torch.float16, device="cuda")
+    F.matmul_nbits(dev(a), dev(b), dev(s), dev(zp), dev(bias), K=K, N=N, block_size=bs, out=big[:, N:2 * N])
+    torch.cuda.synchronize()
+    ref = O.matmul_nbits(a, b, s, zp, bias, K=K, N=N, bits=4, block_size=bs)
+    out = big.cpu().numpy()
+    assert np.all(out[:, :N] == 7.0) and np.all(out[:, 2 * N:] == 7.0)
+    assert within_baseline_tol(out[:, N:2 * N], ref)[0]
+
+
 # ----------------------------------------------------------------- prefill GEMM (tcgen05)
 GEMM_SHAPES = [
     # (M, K, N, bs): ragged M and N tiles, bs 16..128, one and many K steps, several tiles per CTA

@@ -361,6 +361,7 @@ uint64_t gemv_workspace_bytes(const Problem&) { return 0; }
 cudaError_t launch_gemv(const Problem& p, void* /*workspace*/, cudaStream_t stream) {
   if (p.N == 0 || p.M == 0) return cudaSuccess;
   if (gemv_staged_supported(p)) return launch_gemv_staged(p, stream);
+  if (gemv_mr_supported(p)) return launch_gemv_mr(p, stream);
   if (gemv_m1_supported(p)) return launch_gemv_m1(p, stream);
   const GemvShape s = gemv_shape(p);
   GemvParams gp{};

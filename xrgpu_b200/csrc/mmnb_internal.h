@@ -58,6 +58,10 @@ struct StagedPush {
 };
 cudaError_t launch_gemv_staged_push(const Problem& p, const StagedPush* push, cudaStream_t s);
 
+// Its multi-row form (1..16 rows, block size 128 or 256), weights staged like the single-row form.
+bool gemv_mr_supported(const Problem& p);
+cudaError_t launch_gemv_mr(const Problem& p, cudaStream_t s);
+
 // 4-bit prefill GEMM on tcgen05 tensor cores (sm_100a), float16 activations.
 bool gemm_supported(const Problem& p);
 uint64_t gemm_workspace_bytes(const Problem& p);
