@@ -260,6 +260,11 @@ XRGPU_API int xrgpu_p2p_forward_recv(xrgpu_p2p* group, int64_t shard_cols, void*
 XRGPU_API int xrgpu_p2p_forward_recv_many(int32_t count, xrgpu_p2p* const* groups, const int64_t* shard_cols,
                                           void* const* outs, const int64_t* out_valid_cols, void* stream);
 
+/* Identifier of the CUDA graph capture `stream` takes part in (0 when it is not capturing), so a
+ * host can tell whether two enqueues belong to one capture (cross-stream ordering is only legal
+ * inside one). No reference counterpart. */
+XRGPU_API int xrgpu_stream_capture_id(void* stream, uint64_t* id);
+
 /* Unmaps the peers' regions and frees this rank's. Call only after every rank has finished its
  * last all-gather on the group (synchronise, then a host barrier). */
 XRGPU_API int xrgpu_p2p_destroy(xrgpu_p2p* group);

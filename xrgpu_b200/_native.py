@@ -26,6 +26,7 @@ EXPORTED = (
     "xrgpu_mmnb_dequantize", "xrgpu_mmnb_select_path", "xrgpu_device_error", "xrgpu_version",
     "xrgpu_p2p_create", "xrgpu_p2p_connect", "xrgpu_p2p_allgather", "xrgpu_p2p_destroy",
     "xrgpu_p2p_forward_supported", "xrgpu_p2p_forward_send", "xrgpu_p2p_forward_recv", "xrgpu_p2p_forward_recv_many",
+    "xrgpu_stream_capture_id",
     "xrgpu_plan_ex", "xrgpu_prepare_ex", "xrgpu_mlp_workspace_size", "xrgpu_mlp_forward", "xrgpu_mlp_forward_static",
     "xrgpu_qkv_workspace_size",
     "xrgpu_qkv_forward", "xrgpu_bnb4_forward", "xrgpu_gather_block_quantized_forward", "xrgpu_qmoe_workspace_size",
@@ -165,6 +166,7 @@ def load(path: os.PathLike | None = None):
         "xrgpu_p2p_forward_send": ([vp, P(Problem_), ctypes.c_int64, vp, vp], ctypes.c_int),
         "xrgpu_p2p_forward_recv": ([vp, ctypes.c_int64, vp, ctypes.c_int64, vp], ctypes.c_int),
         "xrgpu_p2p_forward_recv_many": ([i32, P(vp), P(ctypes.c_int64), P(vp), P(ctypes.c_int64), vp], ctypes.c_int),
+        "xrgpu_stream_capture_id": ([vp, P(u64)], ctypes.c_int),
         "xrgpu_plan_ex": ([P(RequestEx_), P(Tensor_), i32, P(i32)], ctypes.c_int),
         "xrgpu_prepare_ex": ([ctypes.c_char_p, P(RequestEx_), P(Options_), P(vp)], ctypes.c_int),
         "xrgpu_mlp_workspace_size": ([P(MlpProblem_), P(u64)], ctypes.c_int),

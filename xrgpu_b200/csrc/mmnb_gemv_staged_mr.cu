@@ -134,8 +134,9 @@ __device__ __forceinline__ int owner_of(int i, int base, int r) {
 //   [0, 8 MT xpitch)           activation rows (rows >= M zero), each 16-byte group (x0..x7) stored as
 //                              (x0,x4) (x2,x6) (x1,x5) (x3,x7) at its swizzled position
 //   [.., + upt 8 MT 4)         sums[unit][row] of every 128 activations times 2^-24
-//   [.., + W 2 16 8 MT 4)      partial sums of tiles cut between warps, [warp][first / last][16][8 MT]
-//   [ring_off, ..)             W rings of kNst stages: [16 rows x 256 B][16 x sb scales][16 x zb zero points]
+//   [ring_off, ..)             W rings of kNst stages: [16 rows x 256 B][16 x sb scales][16 x zb zero points];
+//                              after the last stage, partial sums of tiles cut between warps
+//                              [warp][first / last][16][8 MT]
 template <int MT, int ZM, int W>
 __global__ void __launch_bounds__(W * 32, 1) gemv_staged_mr_kernel(const __grid_constant__ MrParams p) {
   constexpr int kRowsPad = 8 * MT;
@@ -145,7 +146,9 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_staged_mr_kernel(const __grid_
   const uint32_t s_base = smem_u32(smem);
   const uint32_t s_x = s_base;
   const uint32_t s_sums = s_x + kRowsPad * p.xpitch;
-  float* red = reinterpret_cast<float*>(smem + kRowsPad * p.xpitch + p.upt * kRowsPad * 4);
+  // partial sums of tiles cut between warps, [warp][first / last][16][8 MT]: in the ring area,
+  // written only after every warp has finished streaming
+  float* red = reinterpret_cast<float*>(smem + p.ring_off);
   const uint32_t s_ring = s_base + p.ring_off + warp * kNst * p.slot_bytes;
 
   const int tile_lo = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.tiles / gridDim.x);
@@ -224,37 +227,42 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_staged_mr_kernel(const __grid_
   for (int j = 0; j < kNst - 1; ++j) issue();
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  {  // Activations: up to eight 16-byte loads per thread in flight; rows >= M are zero. A unit's 16
-     // groups sit on 16 consecutive lanes, whose sums are added with shuffles.
-    constexpr int kBatch = 8;
+  {  // Activations: every 16-byte group copied into place by cp.async (rows >= M zero-filled), then
+     // one pass per (row, unit) turns the unit's 16 groups into MMA order in place -- (x0..x7) to
+     // (x0,x4) (x2,x6) (x1,x5) (x3,x7), the second 8 groups swapped in pairs (the row swizzle keeps
+     // a unit's groups inside the unit) -- and adds its 128 activations. Lanes start at different
+     // groups of their unit so the eight lanes of a phase hit different bank groups.
     const int gpr = p.K / 8;  // 16-byte groups per row
-    const int total = kRowsPad * gpr;
-    for (int base0 = 0; base0 < total; base0 += kThreads * kBatch) {
-      uint4 v[kBatch];
+    for (int gi = threadIdx.x; gi < kRowsPad * gpr; gi += kThreads) {
+      const int row = gi / gpr, idx = gi - row * gpr;
+      const bool real = row < p.M;
+      const void* src = real ? static_cast<const void*>(p.x + static_cast<int64_t>(row) * p.K + 8 * idx) : p.x;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s_x + row * p.xpitch + 16 * idx), "l"(src),
+                   "r"(real ? 16 : 0)
+                   : "memory");
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    for (int ru = threadIdx.x; ru < kRowsPad * p.upt; ru += kThreads) {
+      const int row = ru / p.upt, u = ru - row * p.upt;
+      const uint32_t ub = s_x + row * p.xpitch + 256 * u;
+      float sum = 0.f;
 #pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const int gi = base0 + j * kThreads + static_cast<int>(threadIdx.x);
-        const int row = gi / gpr;
-        v[j] = (gi < total && row < p.M)
-                   ? __ldg(reinterpret_cast<const uint4*>(p.x) + static_cast<int64_t>(row) * gpr + (gi - row * gpr))
-                   : make_uint4(0u, 0u, 0u, 0u);
+      for (int half = 0; half < 2; ++half) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = lds128(ub + 16 * (8 * half + ((j + ru) & 7)));
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int i = 8 * half + ((j + ru) & 7);
+          sum += (hsum2(v[j].x) + hsum2(v[j].y)) + (hsum2(v[j].z) + hsum2(v[j].w));
+          sts128(ub + 16 * x_swizzle(i), make_uint4(prmt(v[j].x, v[j].z, 0x5410), prmt(v[j].y, v[j].w, 0x5410),
+                                                    prmt(v[j].x, v[j].z, 0x7632), prmt(v[j].y, v[j].w, 0x7632)));
+        }
       }
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        if (base0 + j * kThreads >= total) break;  // warp-uniform: total is a multiple of 128
-        const int gi = base0 + j * kThreads + static_cast<int>(threadIdx.x);
-        const int row = gi / gpr, idx = gi - row * gpr;
-        float sum = (hsum2(v[j].x) + hsum2(v[j].y)) + (hsum2(v[j].z) + hsum2(v[j].w));
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        sts128(s_x + row * p.xpitch + 16 * x_swizzle(idx),
-               make_uint4(prmt(v[j].x, v[j].z, 0x5410), prmt(v[j].y, v[j].w, 0x5410), prmt(v[j].x, v[j].z, 0x7632),
-                          prmt(v[j].y, v[j].w, 0x7632)));
-        if ((idx & 15) == 0)
-          asm volatile("st.shared.f32 [%0], %1;" ::"r"(s_sums + 4u * ((idx >> 4) * kRowsPad + row)),
-                       "f"(sum * 5.9604644775390625e-8f)
-                       : "memory");
-      }
+      asm volatile("st.shared.f32 [%0], %1;" ::"r"(s_sums + 4u * (u * kRowsPad + row)), "f"(sum * 5.9604644775390625e-8f)
+                   : "memory");
     }
   }
   __syncthreads();
@@ -338,7 +346,10 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_staged_mr_kernel(const __grid_
       p.y[static_cast<int64_t>(row) * p.ldy + n] = __float2half_rn(v);
     }
   };
-  // Lane (g, c) holds, for tile t, columns g / g + 8 and rows 8t + 2c / 8t + 2c + 1.
+  // Lane (g, c) holds, for tile t, columns g / g + 8 and rows 8t + 2c / 8t + 2c + 1. A segment that
+  // covers only part of its tile (the warp's first and/or last) is kept in registers until the end.
+  float keep0[MT][4], keep1[MT][4];  // the first / last cut segment
+  bool kept0 = false, kept1 = false;
   auto emit = [&](int tile, bool whole, bool first) {
 #pragma unroll
     for (int t = 0; t < MT; ++t) {
@@ -348,15 +359,26 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_staged_mr_kernel(const __grid_
         store(r0 + 1, tile * kRows + g, tot[t][1]);
         store(r0, tile * kRows + g + 8, tot[t][2]);
         store(r0 + 1, tile * kRows + g + 8, tot[t][3]);
-      } else {  // red[warp][slot][column][row]
-        float* mine = red + (warp * 2 + (first ? 0 : 1)) * kRows * kRowsPad;
-        mine[g * kRowsPad + r0] = tot[t][0];
-        mine[g * kRowsPad + r0 + 1] = tot[t][1];
-        mine[(g + 8) * kRowsPad + r0] = tot[t][2];
-        mine[(g + 8) * kRowsPad + r0 + 1] = tot[t][3];
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) tot[t][j] = 0.f;
+      for (int j = 0; j < 4; ++j) {
+        if (!whole && first) keep0[t][j] = tot[t][j];
+        if (!whole && !first) keep1[t][j] = tot[t][j];
+        tot[t][j] = 0.f;
+      }
+    }
+    kept0 |= !whole && first;
+    kept1 |= !whole && !first;
+  };
+  auto spill = [&](int slot, const float (&kv)[MT][4]) {  // red[warp][slot][column][row]
+    float* mine = red + (warp * 2 + slot) * kRows * kRowsPad;
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      const int r0 = 8 * t + 2 * c;
+      mine[g * kRowsPad + r0] = kv[t][0];
+      mine[g * kRowsPad + r0 + 1] = kv[t][1];
+      mine[(g + 8) * kRowsPad + r0] = kv[t][2];
+      mine[(g + 8) * kRowsPad + r0 + 1] = kv[t][3];
     }
   };
   auto finish = [&](int tile) {
@@ -393,6 +415,9 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_staged_mr_kernel(const __grid_
     }
   }
   cp_async_wait<0>();
+  __syncthreads();  // the rings are free: cut-tile partials go there
+  if (kept0) spill(0, keep0);
+  if (kept1) spill(1, keep1);
   __syncthreads();
   if (u_lo < u_hi) {
     finish(tile0);
@@ -409,7 +434,7 @@ struct MrShape {
 MrShape mr_shape(const Problem& p) {
   MrShape s{};
   s.mt = p.M <= 8 ? 1 : 2;
-  s.warps = s.mt == 1 ? 16 : 8;
+  s.warps = s.mt == 1 ? 16 : 11;
   const int win_blocks = static_cast<int>((kWinUnits * kUnitK) / p.bs);  // 4 or 2
   s.sb = 2 * win_blocks;
   s.zb = p.zp == kZpPacked ? win_blocks / 2 : (p.zp == kZpF32 ? 4 * win_blocks : (p.zp == kZpF16 ? 2 * win_blocks : 0));
@@ -418,10 +443,11 @@ MrShape mr_shape(const Problem& p) {
   s.xpitch = static_cast<int>(2 * p.K + 16);
   const int rows_pad = 8 * s.mt;
   const int64_t upt = p.K / kUnitK;
-  const int64_t head = static_cast<int64_t>(rows_pad) * s.xpitch + upt * rows_pad * 4 +
-                       static_cast<int64_t>(s.warps) * 2 * kRows * rows_pad * 4;
+  const int64_t head = static_cast<int64_t>(rows_pad) * s.xpitch + upt * rows_pad * 4;
   s.ring_off = static_cast<int>((head + 255) & ~int64_t{255});
-  s.smem = static_cast<size_t>(s.ring_off) + static_cast<size_t>(s.warps) * kNst * s.slot_bytes;
+  const size_t rings = static_cast<size_t>(s.warps) * kNst * s.slot_bytes;
+  const size_t red = static_cast<size_t>(s.warps) * 2 * kRows * rows_pad * 4;  // aliases the rings
+  s.smem = static_cast<size_t>(s.ring_off) + std::max(rings, red);
   return s;
 }
 
@@ -496,7 +522,7 @@ cudaError_t launch_gemv_mr(const Problem& p, cudaStream_t stream) {
   mp.xpitch = s.xpitch;
   mp.ring_off = s.ring_off;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(device_sm_count(), mp.tiles)));
-  return s.mt == 1 ? launch_mr_mt<1, 16>(p, mp, grid, s.smem, stream) : launch_mr_mt<2, 8>(p, mp, grid, s.smem, stream);
+  return s.mt == 1 ? launch_mr_mt<1, 16>(p, mp, grid, s.smem, stream) : launch_mr_mt<2, 11>(p, mp, grid, s.smem, stream);
 }
 
 }  // namespace xrgpu

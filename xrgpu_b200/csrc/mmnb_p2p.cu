@@ -595,6 +595,18 @@ int xrgpu_p2p_forward_recv(xrgpu_p2p* g, int64_t shard_cols, void* out, int64_t 
   return xrgpu_p2p_forward_recv_many(1, &g, &shard_cols, &out, &out_valid_cols, stream);
 }
 
+int xrgpu_stream_capture_id(void* stream, uint64_t* id) {
+  using namespace xrgpu;
+  if (!id) return api_fail(XRGPU_INVALID_ARGUMENT, "null result pointer");
+  *id = 0;
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  unsigned long long seq = 0;
+  const cudaError_t e = cudaStreamGetCaptureInfo(static_cast<cudaStream_t>(stream), &status, &seq);
+  if (e != cudaSuccess) return api_fail(XRGPU_RUNTIME_ERROR, std::string("cudaStreamGetCaptureInfo failed: ") + cudaGetErrorString(e));
+  if (status == cudaStreamCaptureStatusActive) *id = seq;
+  return XRGPU_OK;
+}
+
 int xrgpu_p2p_destroy(xrgpu_p2p* g) {
   using namespace xrgpu;
   if (!g) return XRGPU_OK;

@@ -29,6 +29,13 @@ from . import _native
 __all__ = ["PeerAllGather"]
 
 
+def _capture_id(stream) -> int:
+    """The CUDA graph capture `stream` belongs to (0: none)."""
+    out = ctypes.c_uint64(0)
+    _native.check(_native.load().xrgpu_stream_capture_id(ctypes.c_void_p(stream.cuda_stream), ctypes.byref(out)))
+    return out.value
+
+
 class PeerAllGather:
     def __init__(self, slot_bytes: int, group=None, device: Optional[torch.device] = None):
         self.group = group
@@ -45,7 +52,7 @@ class PeerAllGather:
                                            ctypes.byref(ptr), handle))
         self._g = ptr
         self.broken = False
-        self._recv_done = None  # (stream, captured) of the last fused receive
+        self._recv_done = None  # (stream, capture id) of the last fused receive
         self._sent = False      # a fused send is waiting for its receive
         self._recv_seq = 0
         handles = [None] * self.world
@@ -128,20 +135,21 @@ class PeerAllGather:
             n, arr(ctypes.c_void_p, [g._g for g in groups]), arr(ctypes.c_int64, [int(it[1]) for it in items]),
             arr(ctypes.c_void_p, [it[2].data_ptr() for it in items]), arr(ctypes.c_int64, [int(it[3]) for it in items]),
             ctypes.c_void_p(stream.cuda_stream)))
-        captured = torch.cuda.is_current_stream_capturing()
+        capture = _capture_id(stream)
         for g in groups:
             g._sent = False
             g._recv_seq += 1
-            g._recv_done = (stream, captured)
+            g._recv_done = (stream, capture)
 
     def _order_after_recv(self, stream) -> None:
         """Make `stream` wait for the stream of the group's last fused receive when that is another
-        stream in the same capture state (a receive captured in another graph must have been joined
-        by the caller, e.g. ShardedMatMulNBits.wait_gather). No event is recorded when the receive
-        and the next call share a stream, so consecutive kernels keep their early launch."""
+        stream of the same graph capture (or both are outside capture). A receive in another capture
+        is ordered by the graphs' own order of replay, one outside capture by the synchronisation
+        that begins a capture. No event is recorded when the receive and the next call share a
+        stream, so consecutive kernels keep their early launch."""
         if self._recv_done is None or self._recv_done[0] == stream:
             return
-        if self._recv_done[1] != torch.cuda.is_current_stream_capturing():
+        if self._recv_done[1] != _capture_id(stream):
             return
         stream.wait_stream(self._recv_done[0])
 
