@@ -279,9 +279,21 @@ class Runner:
         wl, dev, F = self.wl, self.device, self.F
         g = torch.Generator(device=dev)
         g.manual_seed(self.args.seed)
-        self.acts = {K: torch.randn((self.M, K), generator=g, device=dev, dtype=torch.float32).to(self.dt)
-                     for K in sorted({K for (_, K, _) in wl["proj"]})}
-        self.ys = {n: torch.empty((self.M, N), device=dev, dtype=self.dt) for (n, K, N) in self.full_proj}
+        # Activations and outputs are views into one buffer each (offsets padded to 64 elements), so
+        # the end-to-end step moves them with one host-to-device and one device-to-host copy.
+        pad = lambda n: -(-n // 64) * 64  # noqa: E731
+        ks = sorted({K for (_, K, _) in wl["proj"]})
+        self.act_flat = torch.empty(sum(pad(self.M * K) for K in ks), device=dev, dtype=self.dt)
+        self.acts, off = {}, 0
+        for K in ks:
+            self.acts[K] = self.act_flat[off:off + self.M * K].view(self.M, K)
+            self.acts[K].copy_(torch.randn((self.M, K), generator=g, device=dev, dtype=torch.float32))
+            off += pad(self.M * K)
+        self.y_flat = torch.empty(sum(pad(self.M * N) for (_, _, N) in self.full_proj), device=dev, dtype=self.dt)
+        self.ys, off = {}, 0
+        for (n, K, N) in self.full_proj:
+            self.ys[n] = self.y_flat[off:off + self.M * N].view(self.M, N)
+            off += pad(self.M * N)
         self.weights, self.full = [], []
         self.keep_full = min(self.layers, 4) if (self.mode == "strong" and self.world > 1) else 0
         shard_bytes = {}
@@ -484,21 +496,20 @@ class Runner:
 
     def e2e(self, steps, warmup):
         """End to end through the public call: every step copies its activations in from pinned host
-        memory, runs the step's library calls and copies every Y out to pinned host memory, then
-        synchronises. Steps without NCCL calls replay one CUDA graph holding the copies and the calls
-        (recorded through the same public API); the eager form is timed too (e2e_eager_ms)."""
+        memory (one copy: they share one buffer), runs the step's library calls and copies every Y out
+        to pinned host memory (one copy), then synchronises. Steps without NCCL calls replay one CUDA
+        graph holding the copies and the calls (recorded through the same public API); the eager form
+        is timed too (e2e_eager_ms)."""
         import torch
-        host_a = {K: a.cpu().pin_memory() for K, a in self.acts.items()}
-        host_y = {n: torch.empty(y.shape, dtype=y.dtype).pin_memory() for n, y in self.ys.items()}
-        h2d = sum(v.numel() * v.element_size() for v in host_a.values())
-        d2h = sum(v.numel() * v.element_size() for v in host_y.values())
+        host_a = self.act_flat.cpu().pin_memory()
+        host_y = torch.empty(self.y_flat.shape, dtype=self.y_flat.dtype).pin_memory()
+        h2d = host_a.numel() * host_a.element_size()
+        d2h = host_y.numel() * host_y.element_size()
 
         def body(layer):
-            for K, h in host_a.items():
-                self.acts[K].copy_(h, non_blocking=True)
+            self.act_flat.copy_(host_a, non_blocking=True)
             self.step(layer)
-            for n, h in host_y.items():
-                h.copy_(self.ys[n], non_blocking=True)
+            host_y.copy_(self.y_flat, non_blocking=True)
 
         def timed_e2e(graphs):
             for i in range(max(3, warmup)):
