@@ -77,7 +77,11 @@ def _gloo_rank(rank, world, port, results):
                                                  K=K, N=N, block_size=bs, compute=_oracle_compute)
             y2 = mod2(torch.from_numpy(a))
             ref = O.matmul_nbits(a, b, s, zp, bb, K=K, N=N, bits=4, block_size=bs)
-            results[(rank, i)] = (bool(np.array_equal(y.numpy(), ref)), bool(torch.equal(y, y2)), tuple(y.shape))
+            # defer only applies to the peer-memory exchange: on a gloo group Y is complete at once
+            y3 = mod(torch.from_numpy(a), defer=True)
+            mod.wait_gather()
+            same = bool(torch.equal(y, y2)) and bool(torch.equal(y, y3)) and mod._pending is None
+            results[(rank, i)] = (bool(np.array_equal(y.numpy(), ref)), same, tuple(y.shape))
     finally:
         dist.destroy_process_group()
 
